@@ -1,0 +1,57 @@
+"""ctypes binding of the C ABI declared in include/noise_b200.h.
+
+The product path has exactly one implementation: the CUDA kernels in libnoise_b200.so. If the
+library is missing or cannot be loaded, every call raises; nothing falls back to a CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / 'libnoise_b200.so'
+
+NOISE_OK = 0
+STATUS_NAMES = {
+    0: 'ok', 1: 'bad argument', 2: 'launch failed', 3: 'device wait timed out',
+    4: 'workspace too small', 5: 'unsupported configuration',
+}
+
+c_void_p, c_int, c_float, c_int64, c_uint32, c_size_t, c_uint64 = (
+    ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int64, ctypes.c_uint32, ctypes.c_size_t,
+    ctypes.c_uint64)
+
+# name -> (restype, argtypes); the single source of truth for what the Python side binds.
+SIGNATURES: dict[str, tuple] = {
+    'noise_gemm_bf16': (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int,
+                                c_void_p, c_void_p]),
+}
+
+
+class NoiseError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once and attach argument types; raises if it is absent."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise NoiseError(f'{LIB_PATH} is missing: run `python -m noise_b200.build` (or __graft_entry__.build())')
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = lib
+    return _lib
+
+
+def check(code: int, what: str) -> None:
+    if code != NOISE_OK:
+        raise NoiseError(f'{what}: {STATUS_NAMES.get(code, code)}')
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)

@@ -1,0 +1,245 @@
+// Persistent tcgen05 GEMM engine for the population forward: C[M, N] = A[M, K] * B[N, K]^T with
+// bf16 operands in HBM, fp32 accumulators in tensor memory, and a pluggable epilogue that turns each
+// accumulator row into the layer's outputs (rank-1 draw terms, RoPE, norms, residual mixing, ...).
+//
+// Roles (10 warps, one CTA per SM):
+//   warp 0      TMA producer: streams 128x64 A tiles and 256x64 B tiles into a ring of smem stages.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16) into one of two TMEM
+//               accumulators (2 x 256 fp32 columns = all 512 columns), commits stage releases.
+//   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4).. of column half (w-2)/4 and hands 64-column
+//               groups to the epilogue functor, then releases the accumulator.
+// A CTA owns whole M tiles (all N tiles of an M tile run back to back on the same CTA), so per-row
+// state can live in epilogue registers across the N loop and A stays hot in L2 while N advances.
+//
+// Epilogue functor contract (all methods run on every epilogue thread; `row` is global):
+//   static constexpr int kSmemBytes;                 shared memory the functor needs
+//   __device__ Epi(const Params&, uint8_t* smem, int epi_warp, int lane)
+//   __device__ void begin_mtile(int m_tile, int row)
+//   __device__ void begin_tile(int m_tile, int n_tile, int col0)   warp-uniform; may __syncwarp
+//   __device__ void group(int row, int col, float (&v)[64])        64 consecutive columns of `row`
+//   __device__ void end_mtile(int m_tile, int row)
+#pragma once
+
+#include "ptx.cuh"
+
+namespace noise {
+
+struct GemmShape {
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks;
+  int* status;
+};
+
+template <int kStages>
+struct GemmLayout {
+  static constexpr int BM = 128, BN = 256, BK = 64;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = (2 + kEpiWarps) * 32;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kCoreBytes = kStages * kStageBytes + kBarrierBytes;
+};
+
+template <class Epi, int kStages>
+__global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmShape shape, const typename Epi::Params ep) {
+  using L = GemmLayout<kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = base + kStages * L::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * L::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* tfull = bars + 2 * kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* epi_smem = base + L::kCoreBytes;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* status = shape.status;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], L::kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_phase[kStages];
+      bool issued[kStages];
+      for (int s = 0; s < kStages; ++s) issued[s] = false, issued_phase[s] = 0;
+      const uint64_t keep = l2_policy_evict_last();  // weights: every CTA re-reads them
+      bool ok = true;
+      for (int m = blockIdx.x; ok && m < shape.m_tiles; m += gridDim.x) {
+        for (int n = 0; ok && n < shape.n_tiles; ++n) {
+          for (int kb = 0; kb < shape.k_blocks; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+            tma_load_2d(sA + stage * L::kABytes, &tmA, &full[stage], kb * L::BK, m * L::BM);
+            tma_load_2d_hint(sB + stage * L::kBBytes, &tmB, &full[stage], kb * L::BK, n * L::BN, keep);
+            issued[stage] = true;
+            issued_phase[stage] = phase;
+            if (++stage == kStages) stage = 0, phase ^= 1;
+          }
+        }
+      }
+      // Every copy this thread started lands before the CTA can exit.
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s]) mbar_wait(&full[s], issued_phase[s], abort_flag, status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = make_idesc(1, L::BM, L::BN);
+      uint32_t stage = 0, phase = 0, t = 0;
+      bool ok = true;
+      for (int m = blockIdx.x; ok && m < shape.m_tiles; m += gridDim.x) {
+        for (int n = 0; ok && n < shape.n_tiles; ++n, ++t) {
+          const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + acc * L::BN;
+          for (int kb = 0; kb < shape.k_blocks; ++kb) {
+            if (!mbar_wait(&full[stage], phase, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t da = smem_desc_sw128(sA + stage * L::kABytes);
+            const uint64_t db = smem_desc_sw128(sB + stage * L::kBBytes);
+#pragma unroll
+            for (int k = 0; k < L::BK / 16; ++k)
+              tc_mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc_commit(&empty[stage]);
+            if (++stage == kStages) stage = 0, phase ^= 1;
+          }
+          if (ok) tc_commit(&tfull[acc]);
+        }
+      }
+      // No MMA may still be writing TMEM when it is freed.
+      tc_commit(drain);
+      mbar_wait(drain, 0, abort_flag, status);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 2;
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = ew >> 2;      // column half of the 256-wide tile
+    Epi epi(ep, epi_smem, ew, lane);
+    uint32_t t = 0;
+    bool ok = true;
+    for (int m = blockIdx.x; ok && m < shape.m_tiles; m += gridDim.x) {
+      const int row = m * L::BM + quarter * 32 + lane;
+      epi.begin_mtile(m, row);
+      for (int n = 0; n < shape.n_tiles; ++n, ++t) {
+        const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int col0 = half * (L::BN / 2);
+        epi.begin_tile(m, n, n * L::BN + col0);
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * L::BN + col0;
+#pragma unroll 1
+        for (int g = 0; g < L::BN / 2 / 64; ++g) {
+          float v[64];
+          tmem_ld32(taddr + g * 64, *reinterpret_cast<float(*)[32]>(&v[0]));
+          tmem_ld32(taddr + g * 64 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+          if (g == L::BN / 2 / 64 - 1) {
+            // All TMEM reads of this tile are done: hand the accumulator back to the MMA warp.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+          epi.group(row, n * L::BN + col0 + g * 64, v);
+        }
+      }
+      if (ok) epi.end_mtile(m, row);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn();
+int device_sm_count();
+
+// Tensor map of a row-major [rows, cols] matrix read in boxes of box_rows x box_cols elements with
+// 128-byte swizzle (box_cols * element size must be 128 bytes).
+int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
+
+template <class Epi, int kStages>
+int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, int ldb,
+                   const typename Epi::Params& ep, int* status, cudaStream_t stream, int max_ctas = 0) {
+  using L = GemmLayout<kStages>;
+  if (M <= 0 || N <= 0 || K <= 0 || M % L::BM || N % L::BN || K % L::BK) return kStatusBadArgument;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) return kStatusBadArgument;
+  if ((lda * 2) % 16 || (ldb * 2) % 16 || lda < K || ldb < K) return kStatusBadArgument;
+  CUtensorMap ta, tb;
+  if (make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, L::BM, L::BK)) return kStatusBadArgument;
+  if (make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, L::BN, L::BK)) return kStatusBadArgument;
+  GemmShape shape{M, N, K, M / L::BM, N / L::BN, K / L::BK, status};
+  const int smem = 1024 + L::kCoreBytes + Epi::kSmemBytes;
+  static bool configured = false;  // one instantiation = one kernel
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel<Epi, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return kStatusLaunchFailed;
+    configured = true;
+  }
+  int grid = device_sm_count();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (grid > shape.m_tiles) grid = shape.m_tiles;
+  gemm_tc_kernel<Epi, kStages><<<grid, L::kThreads, smem, stream>>>(ta, tb, shape, ep);
+  return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+}  // namespace noise
