@@ -45,7 +45,7 @@ struct GemmLayout {
 template <class Epi, int kStages>
 __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmShape shape, const typename Epi::Params ep) {
+                   const GemmShape shape, const __grid_constant__ typename Epi::Params ep) {
   using L = GemmLayout<kStages>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -1,0 +1,127 @@
+// The fixed model's shapes, the flat parameter layout and the draw-stream tensor ids.
+//
+// Master parameters are one fp32 buffer in `GPT.named_parameters()` order (utils/model.py:123-147:
+// resid_lambdas, x0_lambdas, transformer.wte, blocks h.0..h.7 as c_q, c_k, c_v, c_proj, [ve_gate],
+// c_fc, mlp.c_proj, then lm_head and value_embeds.{1,3,5,7}); the index of a parameter in that order
+// is its draw-stream tensor id. The GEMMs read a packed bf16 copy of the matrices:
+//   per layer: [c_q; c_k; c_v] (1536 x 512) | c_proj (512 x 512) | c_fc (2048 x 512) | mlp.c_proj (512 x 2048)
+//   then lm_head (4096 x 512).
+#pragma once
+
+#include <stdint.h>
+
+#include "philox.cuh"
+
+namespace noise {
+
+constexpr int kLayers = 8, kWidth = 512, kVocab = 4096, kHidden = 2048, kHeads = 8, kHeadDim = 64;
+constexpr int kGateChannels = 32;
+constexpr float kSoftCap = 15.0f;
+constexpr float kNormEps = 1.1920928955078125e-07f;  // float32 epsilon, F.rms_norm's default
+
+__host__ __device__ constexpr bool has_ve(int layer) { return (layer & 1) == 1; }  // utils/model.py:50-52
+__host__ __device__ constexpr int layer_window(int layer) { return (layer % 4 == 3 || layer == kLayers - 1) ? 2048 : 1024; }
+
+// draw-stream tensor ids (= index in named_parameters order)
+constexpr uint32_t kTidResid = 0, kTidX0 = 1, kTidWte = 2, kTidHead = 55;
+__host__ __device__ constexpr uint32_t tid_base(int layer) { return 3 + 6 * layer + layer / 2; }
+__host__ __device__ constexpr uint32_t tid_q(int l) { return tid_base(l); }
+__host__ __device__ constexpr uint32_t tid_k(int l) { return tid_base(l) + 1; }
+__host__ __device__ constexpr uint32_t tid_v(int l) { return tid_base(l) + 2; }
+__host__ __device__ constexpr uint32_t tid_proj(int l) { return tid_base(l) + 3; }
+__host__ __device__ constexpr uint32_t tid_gate(int l) { return tid_base(l) + 4; }
+__host__ __device__ constexpr uint32_t tid_fc(int l) { return tid_base(l) + 4 + (has_ve(l) ? 1 : 0); }
+__host__ __device__ constexpr uint32_t tid_mlp(int l) { return tid_base(l) + 5 + (has_ve(l) ? 1 : 0); }
+__host__ __device__ constexpr uint32_t tid_ve(int l) { return 56 + l / 2; }
+constexpr int kNumTensors = 60;
+
+// Offsets (in floats) of every tensor in the flat master buffer.
+struct ParamLayout {
+  int64_t offset[kNumTensors];
+  int rows[kNumTensors];
+  int cols[kNumTensors];  // 1 for vectors
+  int64_t total;
+};
+
+inline ParamLayout make_param_layout() {
+  ParamLayout L{};
+  int n = 0;
+  auto add = [&](int r, int c) {
+    L.rows[n] = r;
+    L.cols[n] = c;
+    ++n;
+  };
+  add(kLayers, 1);
+  add(kLayers, 1);
+  add(kVocab, kWidth);
+  for (int l = 0; l < kLayers; ++l) {
+    add(kWidth, kWidth);
+    add(kWidth, kWidth);
+    add(kWidth, kWidth);
+    add(kWidth, kWidth);
+    if (has_ve(l)) add(kHeads, kGateChannels);
+    add(kHidden, kWidth);
+    add(kWidth, kHidden);
+  }
+  add(kVocab, kWidth);
+  for (int l = 1; l < kLayers; l += 2) add(kVocab, kWidth);
+  int64_t off = 0;
+  for (int i = 0; i < n; ++i) {
+    L.offset[i] = off;
+    off += (int64_t)L.rows[i] * L.cols[i];
+  }
+  L.total = off;
+  return L;
+}
+
+// packed bf16 GEMM weights
+constexpr int64_t kPackQkv = 0;
+constexpr int64_t kPackProj = 3 * kWidth * kWidth;
+constexpr int64_t kPackFc = kPackProj + kWidth * kWidth;
+constexpr int64_t kPackMlp = kPackFc + (int64_t)kHidden * kWidth;
+constexpr int64_t kPackLayer = kPackMlp + (int64_t)kWidth * kHidden;
+constexpr int64_t kPackHead = kLayers * kPackLayer;
+constexpr int64_t kPackTotal = kPackHead + (int64_t)kVocab * kWidth;
+
+// Everything a kernel needs to place a row of the population batch: rows are ordered
+// (member, sequence, token), member j = member_begin + row / (B * T).
+struct PopCtx {
+  const int* tokens;   // [B, T] input ids
+  const int* targets;  // [B, T] next-token ids
+  int T, B;
+  int64_t member_begin;
+  int pairs;           // antithetic directions P: member j uses direction (j mod 2P) / 2
+  float sigma;         // member j perturbs by +sigma (even j) or -sigma (odd j)
+  PhiloxKey key;
+};
+
+struct RowInfo {
+  uint32_t direction;
+  float sign;
+  int t;    // position in the sequence
+  int tok;  // input token id
+  int tgt;  // target id
+};
+
+__device__ __forceinline__ RowInfo row_info(const PopCtx& c, int64_t row) {
+  RowInfo r;
+  const int64_t seq_rows = (int64_t)c.B * c.T;
+  const int64_t j = c.member_begin + row / seq_rows;
+  const int64_t within = row % seq_rows;
+  r.direction = (uint32_t)((j % (2 * (int64_t)c.pairs)) >> 1);
+  r.sign = (j & 1) ? -c.sigma : c.sigma;
+  r.t = (int)(within % c.T);
+  r.tok = __ldg(c.tokens + within);
+  r.tgt = __ldg(c.targets + within);
+  return r;
+}
+
+// Fill dst[0..127] (per-warp shared memory) with elements e0 .. e0+127 of the stream
+// (tensor, vec, direction); e0 % 4 == 0. Caller brackets with __syncwarp().
+__device__ __forceinline__ void warp_gauss128(float* dst, PhiloxKey key, uint32_t tensor, uint32_t vec,
+                                              uint32_t direction, uint32_t e0, int lane) {
+  const float4 g = gauss4(key, (e0 >> 2) + lane, tensor, vec, direction);
+  reinterpret_cast<float4*>(dst)[lane] = g;
+}
+
+}  // namespace noise

@@ -1,0 +1,300 @@
+// Population forward of the rank-1 (EGGROLL) estimator: the perturbed forward of
+// `population_loss` (train/val/eggroll.py:66-103) for a contiguous range of members, each member
+// evaluating every row of a [B, T] token batch, reduced to one mean cross-entropy per member.
+//
+// Kernel sequence per chunk of members (rows ordered member, sequence, token):
+//   embed            x0 = norm(wte[id] + s a_id b) and block 0's input, with its row statistics
+//   8 x { QKV GEMM   q, k (RoPE + QK-norm), v (+ gated value embedding)
+//         attention  sliding window, writes y and y.b_proj
+//         proj GEMM  x += y Wp^T (+rank-1); FC input + stats
+//         FC GEMM    relu^2 hidden (bf16) + hidden.b_mlp
+//         MLP GEMM   x += hidden Wm^T (+rank-1); next block's mixed input + stats }
+//   head GEMM        soft-capped logits -> per-row log-sum-exp pieces
+//   member loss      mean over the member's B*T rows
+// No noise tensor is ever materialised: every kernel regenerates its draws from (seed, step,
+// direction, tensor).
+#include "attention.cuh"
+#include "epilogues.cuh"
+#include "noise_b200.h"
+
+namespace noise {
+
+// ------------------------------------------------------------------------------------------------
+// embedding + block-0 input
+// ------------------------------------------------------------------------------------------------
+struct EmbedParams {
+  PopCtx ctx;
+  const float* wte;
+  const float* lambdas;  // resid[8] | x0[8]
+  float* x;
+  __nv_bfloat16* xb;
+  float* inv0;
+  float* stats;  // [rows][2][16]
+};
+
+constexpr int kEmbedRows = 64;
+
+__global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ EmbedParams p) {
+  __shared__ float4 sv[4][kWidth / 4];  // b_wte, b_q0, b_k0, b_v0
+  const int64_t row0 = (int64_t)blockIdx.x * kEmbedRows;
+  const RowInfo r0 = row_info(p.ctx, row0);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < 4 * (kWidth / 4); i += blockDim.x) {
+    const int v = i / (kWidth / 4), blk = i % (kWidth / 4);
+    const uint32_t tensor = v == 0 ? kTidWte : v == 1 ? tid_q(0) : v == 2 ? tid_k(0) : tid_v(0);
+    sv[v][blk] = gauss4(p.ctx.key, blk, tensor, 1, r0.direction);
+  }
+  __syncthreads();
+  const float mix = p.lambdas[0] + r0.sign * gauss1(p.ctx.key, 0, kTidResid, 0, r0.direction) + p.lambdas[kLayers] +
+                    r0.sign * gauss1(p.ctx.key, 0, kTidX0, 0, r0.direction);
+  for (int rr = warp; rr < kEmbedRows; rr += 8) {
+    const int64_t row = row0 + rr;
+    const RowInfo ri = row_info(p.ctx, row);
+    const float sa = ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction);
+    const float4* w = reinterpret_cast<const float4*>(p.wte + (size_t)ri.tok * kWidth);
+    float4 e[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c4 = lane + 32 * k;
+      const float4 wv = __ldg(w + c4), bv = sv[0][c4];
+      e[k] = make_float4(wv.x + sa * bv.x, wv.y + sa * bv.y, wv.z + sa * bv.z, wv.w + sa * bv.w);
+      ss += e[k].x * e[k].x + e[k].y * e[k].y + e[k].z * e[k].z + e[k].w * e[k].w;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float i0 = rms_scale(ss, kWidth);
+    float ssx = 0.f, dq = 0.f, dk = 0.f, dv = 0.f;
+    float4* xo = reinterpret_cast<float4*>(p.x + (size_t)row * kWidth);
+    uint2* xbo = reinterpret_cast<uint2*>(p.xb + (size_t)row * kWidth);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c4 = lane + 32 * k;
+      const float4 xi = make_float4(mix * (e[k].x * i0), mix * (e[k].y * i0), mix * (e[k].z * i0), mix * (e[k].w * i0));
+      xo[c4] = xi;
+      ssx += xi.x * xi.x + xi.y * xi.y + xi.z * xi.z + xi.w * xi.w;
+      const float r[4] = {bf16_round(xi.x), bf16_round(xi.y), bf16_round(xi.z), bf16_round(xi.w)};
+      xbo[c4] = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+      const float4 bq = sv[1][c4], bk = sv[2][c4], bvv = sv[3][c4];
+      dq += r[0] * bq.x + r[1] * bq.y + r[2] * bq.z + r[3] * bq.w;
+      dk += r[0] * bk.x + r[1] * bk.y + r[2] * bk.z + r[3] * bk.w;
+      dv += r[0] * bvv.x + r[1] * bvv.y + r[2] * bvv.z + r[3] * bvv.w;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      ssx += __shfl_xor_sync(0xffffffffu, ssx, o);
+      dq += __shfl_xor_sync(0xffffffffu, dq, o);
+      dk += __shfl_xor_sync(0xffffffffu, dk, o);
+      dv += __shfl_xor_sync(0xffffffffu, dv, o);
+    }
+    const float vals[4] = {ssx, dq, dk, dv};
+    p.stats[(size_t)row * 2 * kStatStride + lane] = lane < 4 ? vals[lane] : 0.f;
+    if (lane == 0) p.inv0[row] = i0;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// per-member mean cross-entropy from the head's per-row pieces
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) member_loss_kernel(const float* part, int64_t rows_per_member, float* losses) {
+  const int m = blockIdx.x;
+  const float* pm = part + (size_t)m * rows_per_member * 4;
+  double acc = 0.0;
+  for (int64_t r = threadIdx.x; r < rows_per_member; r += blockDim.x) {
+    const float4 q = reinterpret_cast<const float4*>(pm)[r];
+    acc += (double)(logf(q.x + q.z) + kSoftCap - (q.y + q.w));
+  }
+  __shared__ double red[256];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = 128; s; s >>= 1) {
+    if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) losses[m] = (float)(red[0] / (double)rows_per_member);
+}
+
+// ------------------------------------------------------------------------------------------------
+// master fp32 -> packed bf16 GEMM weights
+// ------------------------------------------------------------------------------------------------
+struct PackJob {
+  int64_t src, dst, n;
+};
+constexpr int kMaxPackJobs = 8 * 6 + 1;
+struct PackJobs {
+  PackJob job[kMaxPackJobs];
+  int count;
+};
+
+__global__ void pack_weights_kernel(const float* __restrict__ params, __nv_bfloat16* __restrict__ packed,
+                                    const __grid_constant__ PackJobs jobs) {
+  const PackJob j = jobs.job[blockIdx.y];
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < j.n; i += (int64_t)gridDim.x * blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(params + j.src + i);
+    *reinterpret_cast<uint2*>(packed + j.dst + i) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+PackJobs make_pack_jobs() {
+  const ParamLayout L = make_param_layout();
+  PackJobs jobs{};
+  auto add = [&](uint32_t tid, int64_t dst) {
+    jobs.job[jobs.count++] = PackJob{L.offset[tid], dst, (int64_t)L.rows[tid] * L.cols[tid]};
+  };
+  for (int l = 0; l < kLayers; ++l) {
+    const int64_t b = l * kPackLayer;
+    add(tid_q(l), b + kPackQkv);
+    add(tid_k(l), b + kPackQkv + kWidth * kWidth);
+    add(tid_v(l), b + kPackQkv + 2 * kWidth * kWidth);
+    add(tid_proj(l), b + kPackProj);
+    add(tid_fc(l), b + kPackFc);
+    add(tid_mlp(l), b + kPackMlp);
+  }
+  add(kTidHead, kPackHead);
+  return jobs;
+}
+
+// ------------------------------------------------------------------------------------------------
+// workspace
+// ------------------------------------------------------------------------------------------------
+struct PopWorkspace {
+  float* x;
+  __nv_bfloat16* xb;
+  __nv_bfloat16* qkv;
+  __nv_bfloat16* y;
+  __nv_bfloat16* hidden;
+  float* st_a;
+  float* st_b;
+  float* ystats;
+  float* hstats;
+  float* inv0;
+  float* part;
+};
+
+// bytes per row of each buffer, in carve order
+static const size_t kRowBytes[] = {
+    kWidth * 4, kWidth * 2, 3 * kWidth * 2, kWidth * 2, kHidden * 2, 2 * kStatStride * 4, 2 * kStatStride * 4,
+    kHeads * 4, 2 * 4, 4, 4 * 4};
+
+size_t pop_workspace_bytes(int64_t rows) {
+  size_t total = 0;
+  for (size_t b : kRowBytes) total += ((b * rows + 255) / 256) * 256;
+  return total;
+}
+
+PopWorkspace carve(void* ws, int64_t rows) {
+  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
+  void* out[11];
+  for (int i = 0; i < 11; ++i) {
+    out[i] = p;
+    p += ((kRowBytes[i] * rows + 255) / 256) * 256;
+  }
+  return PopWorkspace{(float*)out[0], (__nv_bfloat16*)out[1], (__nv_bfloat16*)out[2], (__nv_bfloat16*)out[3],
+                      (__nv_bfloat16*)out[4], (float*)out[5], (float*)out[6], (float*)out[7], (float*)out[8],
+                      (float*)out[9], (float*)out[10]};
+}
+
+constexpr int kGemmStages = 4;
+
+int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& w, int64_t rows, int layer,
+                     int* status, cudaStream_t stream) {
+  CUtensorMap tm;
+  if (make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, kAttnTile, kHeadDim))
+    return kStatusBadArgument;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(attention_window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem) !=
+        cudaSuccess)
+      return kStatusLaunchFailed;
+    configured = true;
+  }
+  AttnParams ap{ctx, w.y, w.ystats, layer, layer_window(layer), status};
+  dim3 grid(ctx.T / kAttnTile, kHeads, (unsigned)(rows / ctx.T));
+  attention_window_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tm, ap);
+  return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const float* rope, const PopCtx& ctx,
+                      int members, float* losses, PopWorkspace& w, int* status, cudaStream_t stream) {
+  static const ParamLayout L = make_param_layout();
+  const int64_t rows = (int64_t)members * ctx.B * ctx.T;
+  const float* wte = params + L.offset[kTidWte];
+  const float* lambdas = params + L.offset[kTidResid];  // resid_lambdas then x0_lambdas, contiguous
+  int rc;
+  {
+    EmbedParams ep{ctx, wte, lambdas, w.x, w.xb, w.inv0, w.st_a};
+    embed_kernel<<<(unsigned)(rows / kEmbedRows), 256, 0, stream>>>(ep);
+    if (cudaGetLastError() != cudaSuccess) return kStatusLaunchFailed;
+  }
+  for (int l = 0; l < kLayers; ++l) {
+    const __nv_bfloat16* wl = packed + l * kPackLayer;
+    EpiQkv::Params q{ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
+    if ((rc = launch_gemm_tc<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
+                                                  q, status, stream)))
+      return rc;
+    if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
+    EpiProj::Params pp{ctx, w.x, w.xb, w.ystats, w.st_b, l};
+    if ((rc = launch_gemm_tc<EpiProj, kGemmStages>(w.y, wl + kPackProj, (int)rows, kWidth, kWidth, kWidth, kWidth, pp,
+                                                   status, stream)))
+      return rc;
+    EpiFc::Params fp{ctx, w.hidden, w.st_b, w.hstats, l};
+    if ((rc = launch_gemm_tc<EpiFc, kGemmStages>(w.xb, wl + kPackFc, (int)rows, kHidden, kWidth, kWidth, kWidth, fp,
+                                                 status, stream)))
+      return rc;
+    const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
+    EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next, l};
+    if ((rc = launch_gemm_tc<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
+                                                     kHidden, mp, status, stream)))
+      return rc;
+  }
+  EpiHead::Params hp{ctx, w.st_a, w.part};
+  if ((rc = launch_gemm_tc<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
+                                                 hp, status, stream)))
+    return rc;
+  member_loss_kernel<<<members, 256, 0, stream>>>(w.part, (int64_t)ctx.B * ctx.T, losses);
+  return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+}  // namespace noise
+
+using namespace noise;
+
+extern "C" size_t noise_pop_workspace_bytes(int64_t rows) { return pop_workspace_bytes(rows); }
+
+extern "C" int64_t noise_param_count(void) { return make_param_layout().total; }
+
+extern "C" int64_t noise_packed_count(void) { return kPackTotal; }
+
+extern "C" int noise_pack_weights(const float* params, void* packed, void* stream) {
+  static const PackJobs jobs = make_pack_jobs();
+  dim3 grid(64, jobs.count);
+  pack_weights_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      params, reinterpret_cast<__nv_bfloat16*>(packed), jobs);
+  return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+extern "C" int noise_pop_forward_lowrank(const float* params, const void* packed, const float* rope,
+                                         const int32_t* tokens, const int32_t* targets, int B, int T,
+                                         int64_t member_begin, int members, int pairs, float sigma, uint32_t seed,
+                                         uint32_t step, float* losses, void* workspace, size_t workspace_bytes,
+                                         int* status, void* stream) {
+  if (!params || !packed || !rope || !tokens || !targets || !losses || !workspace) return kStatusBadArgument;
+  if (B <= 0 || T <= 0 || T % kAttnTile || ((int64_t)B * T) % 128 || members <= 0 || pairs <= 0 ||
+      member_begin < 0 || T > 20480)
+    return kStatusBadArgument;
+  const int64_t rows_per_member = (int64_t)B * T;
+  int chunk = members;
+  while (chunk > 0 && pop_workspace_bytes(rows_per_member * chunk) > workspace_bytes) --chunk;
+  if (chunk == 0) return kStatusWorkspaceTooSmall;
+  while ((int64_t)chunk * rows_per_member > (int64_t)1 << 30) --chunk;  // int32 row indices in the GEMM
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int m0 = 0; m0 < members; m0 += chunk) {
+    const int mc = members - m0 < chunk ? members - m0 : chunk;
+    PopCtx ctx{tokens, targets, T, B, member_begin + m0, pairs, sigma, PhiloxKey{seed, step}};
+    PopWorkspace w = carve(workspace, rows_per_member * mc);
+    const int rc = pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, mc,
+                                     losses + m0, w, status, s);
+    if (rc) return rc;
+  }
+  return kStatusOk;
+}
