@@ -1,0 +1,313 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 EGGROLL ES update (weak-scaled over N GPUs).
+
+One step = one full ES update: population forward of 1024 rank-1 antithetic members per GPU
+(512 directions per GPU, sigma 1e-3), every member on the same 8 Zipf(1.1) sequences x 2048 tokens,
+per-member CE losses, NCCL all-gather of losses (N > 1), centred-rank fitness, Sigma f eps
+reconstruction fused with AdamW (lr 1e-3), packed-weight refresh.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this repository's CUDA path
+    python bench.py --impl reference [...]                   # the CPU restatement of the reference path
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = 'member-tokens/sec/GPU (pop 16k) and seconds per ES update at 1/2/4/8 B200'
+UNIT = 'member-tokens/s'
+PUBLISHED_PER_GPU = 2.13e6  # EGGROLL w/ Adam on 8xH100, derived member-tokens/s/GPU
+SEQ, BATCH = 2048, 8
+# Algorithmic FLOPs per member-token of each kernel kind over one forward (SURVEY 8d FLOP model):
+# per block q,k,v,proj,fc,mlp GEMMs; attention QK+PV over visible keys only (avg keys per query
+# 768.75 for the 1024-token windows, 1024.5 for the full ones); head 512 x 4096.
+FLOPS_PER_TOKEN = {
+    'qkv': 8 * 2 * 512 * 1536, 'attention': 6 * 2048 * 768.75 + 2 * 2048 * 1024.5, 'proj': 8 * 2 * 512 * 512,
+    'fc': 8 * 2 * 512 * 2048, 'mlp': 8 * 2 * 2048 * 512, 'head': 2 * 512 * 4096,
+}
+FORWARD_FLOPS_PER_TOKEN = sum(FLOPS_PER_TOKEN.values())  # 68,168,704
+KINDS = ['embed', 'qkv', 'attention', 'proj', 'fc', 'mlp', 'head', 'loss', 'fitness', 'update', 'pack', 'other']
+
+
+def load_peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d['bf16_tflops'], d.get('bf16_tflops_sustained', d['bf16_tflops']), d['hbm_gbs'], 'measured'
+    return 1590.0, 1400.0, 6650.0, 'fallback'
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+            target = uuid if uuid.startswith('GPU-') else f'GPU-{uuid}'
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-i', target, '-lms', '200'], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except (OSError, RuntimeError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith('active'):
+                    reasons.add(name)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def dist_setup():
+    rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    return rank, world, local
+
+
+def reference_sample(members: int = 2, length: int = SEQ, steps: int = 1):
+    """Time the CPU restatement of the reference's population forward (oracle port) on the host."""
+    from noise_b200.data import zipf_tokens
+    from oracle import eggroll as oe
+    from oracle import model as om
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    params = om.make_params(0)
+    rows = zipf_tokens(1, length + 1, seed=1)
+    draws, sign = oe.member_draws(list(range(members)), members // 2, 1e-3, 0, 1)
+    times = []
+    with torch.no_grad():
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            om.population_losses(params, draws, sign, rows[:, :-1], rows[:, 1:])
+            times.append(time.perf_counter() - t0)
+    return members * length, times, cores
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    sample = f'{2} members x 1 sequence x {SEQ} tokens of the rank-1 population forward (fp32 CPU oracle port)'
+    tok, times, cores = reference_sample(2, SEQ, args.warmup + args.steps)
+    timed = times[args.warmup:] or times
+    per_step = sum(timed) / len(timed)
+    value = tok / per_step
+    line = {
+        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': len(timed),
+        'warmup': args.warmup, 'ms_per_step': per_step * 1e3, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic Zipf(1.1) tokens, seed-0 random init',
+        'config': workload_config(world, args),
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port', 'sample': sample},
+        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(world, args):
+    return {'workload': 'eggroll-rank1-antithetic', 'members_per_gpu': 2 * args.pairs_per_gpu,
+            'pairs': args.pairs_per_gpu * world, 'sigma': args.sigma, 'sequences_per_member': BATCH,
+            'seq_len': SEQ, 'fitness': 'centered_rank', 'optimizer': 'adamw lr 1e-3 betas (0.5, 0.95)',
+            'parallelism': f'members sharded dp{world}', 'operands': 'bf16 GEMM operands, fp32 accumulate/head/CE',
+            'l2': 'inputs larger than L2 (activations streamed per chunk, GBs)'}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=5)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='noise', choices=['noise', 'reference'])
+    ap.add_argument('--pairs-per-gpu', type=int, default=512)
+    ap.add_argument('--sigma', type=float, default=1e-3)
+    ap.add_argument('--workspace-gb', type=float, default=32.0)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    rank, world, local = dist_setup()
+    if args.impl == 'reference':
+        run_reference(args, rank, world)
+        return
+
+    from noise_b200 import _lib, population
+    from noise_b200.data import zipf_tokens
+    from noise_b200.eggroll import BETAS, AdamW, Eggroll
+    from noise_b200.model import Weights
+
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+    population.DEFAULT_WORKSPACE_BYTES = int(args.workspace_gb * (1 << 30))
+    lib = _lib.load()
+
+    pairs = args.pairs_per_gpu * world
+    members_total = 2 * pairs
+    w = Weights(dev, seed=0)
+    opt = AdamW(w, lr=1e-3, betas=BETAS)
+    es = Eggroll(w, pairs, rank, world, sigma=args.sigma, seed=0, fitness='centered_rank', all_sequences=True)
+    rows = zipf_tokens(BATCH, SEQ + 1, seed=1)
+    rows_dev = rows.to(dev)
+    x, y = rows_dev[:, :-1], rows_dev[:, 1:]
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    step = 0
+    for _ in range(args.warmup):
+        step += 1
+        es.step(x, y, opt, step)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region ----
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.noise_launch_count()
+    _lib.call('noise_profile_enable', 1)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step += 1
+            es.step(x, y, opt, step)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launches = lib.noise_launch_count() - launches0
+    ms_kind = (ctypes_array('d', len(KINDS)), ctypes_array('q', len(KINDS)))
+    _lib.call('noise_profile_read', ms_kind[0].buffer_info()[0], ms_kind[1].buffer_info()[0], len(KINDS))
+    _lib.call('noise_profile_enable', 0)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms, float(launches)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t[:1].clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        sm = t[1:].clone()
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        ms, launches = mx.item(), int(sm.item())
+    tokens_per_step = members_total * BATCH * SEQ
+    value = tokens_per_step / (ms / 1e3)
+
+    # ---- end to end through the public API, host buffers ----
+    host = rows.pin_memory()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    ev2.record(stream)
+    for _ in range(args.steps):
+        step += 1
+        rows_dev.copy_(host, non_blocking=True)
+        es.step(rows_dev[:, :-1], rows_dev[:, 1:], opt, step)  # returns the mean loss on the host
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = ev2.elapsed_time(ev3) / args.steps
+    if world > 1:
+        te = torch.tensor([ms_e2e], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = te.item()
+
+    # ---- roofline of the dominant kernel, from the live per-kind events ----
+    peak_burst, peak_sustained, hbm, peak_kind = load_peaks()
+    kind_ms = {k: ms_kind[0][i] for i, k in enumerate(KINDS)}
+    kind_n = {k: ms_kind[1][i] for i, k in enumerate(KINDS)}
+    local_tokens = (members_total // world) * BATCH * SEQ * args.steps
+    dominant = max(FLOPS_PER_TOKEN, key=lambda k: kind_ms[k])
+    achieved = FLOPS_PER_TOKEN[dominant] * local_tokens / (kind_ms[dominant] / 1e3) / 1e12
+    fwd_ms = sum(kind_ms[k] for k in ('embed', 'qkv', 'attention', 'proj', 'fc', 'mlp', 'head', 'loss'))
+    fwd_tflops = FORWARD_FLOPS_PER_TOKEN * local_tokens / (fwd_ms / 1e3) / 1e12
+    roofline = {
+        'bound': 'tensor', 'kernel': dominant, 'achieved': achieved, 'peak': peak_sustained, 'unit': 'TFLOP/s',
+        'frac': achieved / peak_sustained, 'peak_source': f'{peak_kind} bf16_tflops_sustained',
+        'traffic': TRAFFIC_PER_LAUNCH.get(dominant),
+        'launches': kind_n[dominant], 'ms_per_launch': kind_ms[dominant] / max(1, kind_n[dominant]),
+        'population_forward': {'achieved': fwd_tflops, 'frac': fwd_tflops / peak_sustained,
+                               'frac_of_burst': fwd_tflops / peak_burst},
+        'kernel_ms_per_step': {k: round(kind_ms[k] / args.steps, 3) for k in KINDS if kind_n[k]},
+    }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tok, times, cores = reference_sample(2, SEQ, 2)
+        cpu = {'value': tok / min(times), 'unit': UNIT, 'cores': cores, 'kind': 'port',
+               'sample': '2 members x 1 sequence x 2048 tokens of the rank-1 population forward (fp32 CPU oracle port)'}
+
+    if rank == 0:
+        clk = clocks.summary()
+        line = {
+            'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': (value / world) / PUBLISHED_PER_GPU, 'dtype': 'bf16',
+            'data': 'synthetic Zipf(1.1) tokens, seed-0 random init (FineWeb unavailable offline)',
+            'config': workload_config(world, args),
+            'per_gpu': value / world, 's_per_update': ms / 1e3,
+            'e2e': {'value': tokens_per_step / (ms_e2e / 1e3), 'unit': UNIT,
+                    'h2d_bytes_per_step': host.numel() * host.element_size(), 'd2h_bytes_per_step': 4},
+            'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': cpu,
+            'clocks': {'sm_mhz': clk['sm_mhz'], 'sm_max_mhz': clk['sm_max_mhz'], 'reasons': clk['reasons']},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# dram bytes per launch of each kind from ncu captures (profiles/), scaled to the bench's launch size
+TRAFFIC_PER_LAUNCH: dict = {}
+
+
+def ctypes_array(code, n):
+    import array
+    return array.array(code, [0] * n)
+
+
+if __name__ == '__main__':
+    main()

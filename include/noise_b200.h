@@ -58,6 +58,36 @@ int noise_pop_forward_lowrank(const float* params, const void* packed, const flo
                               float sigma, uint32_t seed, uint32_t step, float* losses, void* workspace,
                               size_t workspace_bytes, int* status, void* stream);
 
+/* Scratch bytes noise_fitness needs for `members` losses. */
+size_t noise_fitness_workspace_bytes(int members);
+
+/* Replaces train/val/eggroll.py:151-154. losses[members] (members even; member 2i+1 is the antithetic
+ * partner of 2i) -> weights[pairs]. mode 0: z-scored pair differences L[2i+1] - L[2i] over their
+ * unbiased std + 1e-8 (the reference); mode 1: differences of centred ranks rank/(N-1) - 0.5 with
+ * ranks ascending, NaN last, ties by member index. Pair i contributes to direction i mod pairs.
+ * ranks (optional, [members] int32) receives the exact ranks. */
+int noise_fitness(const float* losses, int members, int pairs, int mode, float* weights, int32_t* ranks,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces train/val/eggroll.py:155-167 plus torch.optim.AdamW.step (:205): for every parameter
+ * tensor g = -grad_scale * sum_d weights[d] a_d b_d^T (eps_d for the mixing scalars), regenerated
+ * from the (seed, step) stream, then one AdamW step (lr * lr_mult[tensor] if lr_mult != NULL,
+ * betas, eps, decoupled weight_decay, bias corrections for step adam_t) on params/exp_avg/exp_avg_sq,
+ * refreshing the packed bf16 copy when packed != NULL. adam_t == 0 only writes g to grad_out
+ * (37,749,776 floats, optional otherwise). */
+int noise_update_sum_fe_adamw(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* weights,
+                              int pairs, float grad_scale, uint32_t seed, uint32_t step, const float* lr_mult,
+                              float lr, float beta1, float beta2, float eps, float weight_decay, int adam_t,
+                              float* grad_out, void* stream);
+
+/* Instrumentation, no reference counterpart: total kernel launches made by this library so far;
+ * optional per-kind device timing with CUDA events recorded on the launching stream (kinds: 0 embed,
+ * 1 qkv, 2 attention, 3 proj, 4 fc, 5 mlp, 6 head, 7 loss, 8 fitness, 9 update, 10 pack, 11 other).
+ * noise_profile_read synchronises on the recorded events and sums per kind. */
+int64_t noise_launch_count(void);
+int noise_profile_enable(int on);
+int noise_profile_read(double* ms, int64_t* count, int kinds);
+
 #ifdef __cplusplus
 }
 #endif

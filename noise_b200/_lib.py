@@ -31,6 +31,14 @@ SIGNATURES: dict[str, tuple] = {
     'noise_pop_forward_lowrank': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int64,
                                           c_int, c_int, c_float, c_uint32, c_uint32, c_void_p, c_void_p, c_size_t,
                                           c_void_p, c_void_p]),
+    'noise_fitness_workspace_bytes': (c_size_t, [c_int]),
+    'noise_fitness': (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    'noise_update_sum_fe_adamw': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_uint32,
+                                          c_uint32, c_void_p, c_float, c_float, c_float, c_float, c_float, c_int,
+                                          c_void_p, c_void_p]),
+    'noise_launch_count': (c_int64, []),
+    'noise_profile_enable': (c_int, [c_int]),
+    'noise_profile_read': (c_int, [c_void_p, c_void_p, c_int]),
 }
 
 

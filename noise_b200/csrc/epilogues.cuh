@@ -90,11 +90,18 @@ struct EpiQkv {
 #pragma unroll
     for (int j = 0; j < 64; ++j) v[j] = inv * (v[j] + c2 * a[j]);
     if (which < 2) {
-      const float* cs = p.rope + (size_t)ri.t * 64;
+      const float4* cs = reinterpret_cast<const float4*>(p.rope + (size_t)ri.t * 64);
+      float cr[32], sr[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 c4 = __ldg(cs + j), s4 = __ldg(cs + 8 + j);
+        cr[4 * j] = c4.x, cr[4 * j + 1] = c4.y, cr[4 * j + 2] = c4.z, cr[4 * j + 3] = c4.w;
+        sr[4 * j] = s4.x, sr[4 * j + 1] = s4.y, sr[4 * j + 2] = s4.z, sr[4 * j + 3] = s4.w;
+      }
       float ss = 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float c = __ldg(cs + j), s = __ldg(cs + 32 + j);
+        const float c = cr[j], s = sr[j];
         const float x1 = v[j], x2 = v[j + 32];
         v[j] = x1 * c + x2 * s;
         v[j + 32] = x2 * c - x1 * s;
@@ -167,18 +174,22 @@ struct EpiProj {
   __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
     const float* b = vec + 128 + (col & 127);
-    float* xr = p.x + (size_t)row * kWidth + col;
-    __nv_bfloat16* xo = p.xb + (size_t)row * kWidth + col;
+    float* __restrict__ xr = p.x + (size_t)row * kWidth + col;
+    __nv_bfloat16* __restrict__ xo = p.xb + (size_t)row * kWidth + col;
+    // all loads of the row segment first, so they are in flight together
+    float4 x4[16];
 #pragma unroll
-    for (int j = 0; j < 64; j += 4) {
-      float4 x4 = *reinterpret_cast<float4*>(xr + j);
-      x4.x += v[j] + c2 * a[j];
-      x4.y += v[j + 1] + c2 * a[j + 1];
-      x4.z += v[j + 2] + c2 * a[j + 2];
-      x4.w += v[j + 3] + c2 * a[j + 3];
-      *reinterpret_cast<float4*>(xr + j) = x4;
-      v[j] = x4.x, v[j + 1] = x4.y, v[j + 2] = x4.z, v[j + 3] = x4.w;
+    for (int j = 0; j < 16; ++j) x4[j] = reinterpret_cast<const float4*>(xr)[j];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[4 * j] += x4[j].x + c2 * a[4 * j];
+      v[4 * j + 1] += x4[j].y + c2 * a[4 * j + 1];
+      v[4 * j + 2] += x4[j].z + c2 * a[4 * j + 2];
+      v[4 * j + 3] += x4[j].w + c2 * a[4 * j + 3];
     }
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      reinterpret_cast<float4*>(xr)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
       ssq += v[j] * v[j];
@@ -322,33 +333,45 @@ struct EpiMlpOut {
   __device__ void group(int row, int col, float (&v)[64]) {
     const int c = col & 127;
     const float* a = vec + c;
-    float* xr = p.x + (size_t)row * kWidth + col;
-    __nv_bfloat16* xo = p.xb + (size_t)row * kWidth + col;
+    float* __restrict__ xr = p.x + (size_t)row * kWidth + col;
+    __nv_bfloat16* __restrict__ xo = p.xb + (size_t)row * kWidth + col;
+    {
+      float4 x4[16];
 #pragma unroll
-    for (int j = 0; j < 64; j += 4) {
-      const float4 x4 = *reinterpret_cast<const float4*>(xr + j);
-      v[j] = x4.x + v[j] + c2 * a[j];
-      v[j + 1] = x4.y + v[j + 1] + c2 * a[j + 1];
-      v[j + 2] = x4.z + v[j + 2] + c2 * a[j + 2];
-      v[j + 3] = x4.w + v[j + 3] + c2 * a[j + 3];
+      for (int j = 0; j < 16; ++j) x4[j] = reinterpret_cast<const float4*>(xr)[j];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[4 * j] += x4[j].x + c2 * a[4 * j];
+        v[4 * j + 1] += x4[j].y + c2 * a[4 * j + 1];
+        v[4 * j + 2] += x4[j].z + c2 * a[4 * j + 2];
+        v[4 * j + 3] += x4[j].w + c2 * a[4 * j + 3];
+      }
     }
     if (!last) {
       const float* bw = vec + 128 + c;
       const float* bq = vec + 256 + c;
       const float* bk = vec + 384 + c;
       const float* bv = vec + 512 + c;
-      const float* e = p.wte + (size_t)ri.tok * kWidth + col;
+      const float* __restrict__ e = p.wte + (size_t)ri.tok * kWidth + col;
 #pragma unroll
-      for (int j = 0; j < 64; j += 4) {
-        const float4 e4 = __ldg(reinterpret_cast<const float4*>(e + j));
-        const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+      for (int h = 0; h < 64; h += 32) {
+        float4 e4[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float x0 = (ev[u] + sa_wte * bw[j + u]) * i0;
-          v[j + u] = lr * v[j + u] + l0 * x0;
+        for (int j = 0; j < 8; ++j) e4[j] = __ldg(reinterpret_cast<const float4*>(e + h) + j);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float ev[4] = {e4[j].x, e4[j].y, e4[j].z, e4[j].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = h + 4 * j + u;
+            const float x0 = (ev[u] + sa_wte * bw[k]) * i0;
+            v[k] = lr * v[k] + l0 * x0;
+          }
         }
-        *reinterpret_cast<float4*>(xr + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        reinterpret_cast<float4*>(xr)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
         ssq += v[j] * v[j];

@@ -43,5 +43,5 @@ extern "C" int noise_gemm_bf16(const void* A, const void* B, void* C, int M, int
                                int out_bf16, int* status, void* stream) {
   noise::EpiStore::Params ep{C, N, alpha, out_bf16};
   return noise::launch_gemm_tc<noise::EpiStore, 4>(A, B, M, N, K, K, K, ep, status,
-                                                   reinterpret_cast<cudaStream_t>(stream));
+                                                   reinterpret_cast<cudaStream_t>(stream), noise::kKindOther);
 }

@@ -20,6 +20,7 @@
 //   __device__ void end_mtile(int m_tile, int row)
 #pragma once
 
+#include "profile.cuh"
 #include "ptx.cuh"
 
 namespace noise {
@@ -218,7 +219,8 @@ int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, i
 
 template <class Epi, int kStages>
 int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, int ldb,
-                   const typename Epi::Params& ep, int* status, cudaStream_t stream, int max_ctas = 0) {
+                   const typename Epi::Params& ep, int* status, cudaStream_t stream, int kind = kKindOther,
+                   int max_ctas = 0) {
   using L = GemmLayout<kStages>;
   if (M <= 0 || N <= 0 || K <= 0 || M % L::BM || N % L::BN || K % L::BK) return kStatusBadArgument;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) return kStatusBadArgument;
@@ -238,6 +240,7 @@ int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, i
   int grid = device_sm_count();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (grid > shape.m_tiles) grid = shape.m_tiles;
+  LaunchScope scope(kind, stream);
   gemm_tc_kernel<Epi, kStages><<<grid, L::kThreads, smem, stream>>>(ta, tb, shape, ep);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }

@@ -43,3 +43,83 @@ int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, i
 }
 
 }  // namespace noise
+
+// ------------------------------------------------------------------------------------------------
+// Launch accounting and optional per-kernel timing. Every kernel launch of the library goes through
+// LaunchScope, which counts it and, while profiling is on, brackets it with CUDA events on the
+// launching stream so the host can read per-kind device times afterwards.
+// ------------------------------------------------------------------------------------------------
+#include <atomic>
+#include <vector>
+
+#include "profile.cuh"
+
+namespace noise {
+
+static std::atomic<long long> g_launches{0};
+
+struct ProfRecord {
+  int kind;
+  cudaEvent_t a, b;
+};
+
+static struct {
+  std::mutex mu;
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  std::vector<ProfRecord> recs;
+} g_prof;
+
+static cudaEvent_t pool_event() {
+  if (g_prof.used == g_prof.pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    g_prof.pool.push_back(e);
+  }
+  return g_prof.pool[g_prof.used++];
+}
+
+LaunchScope::LaunchScope(int kind, cudaStream_t s) : kind_(kind), s_(s), idx_(-1) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (!g_prof.on) return;
+  ProfRecord r{kind, pool_event(), pool_event()};
+  cudaEventRecord(r.a, s);
+  idx_ = (int)g_prof.recs.size();
+  g_prof.recs.push_back(r);
+}
+
+LaunchScope::~LaunchScope() {
+  if (idx_ < 0) return;
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  cudaEventRecord(g_prof.recs[idx_].b, s_);
+}
+
+}  // namespace noise
+
+using namespace noise;
+
+extern "C" int64_t noise_launch_count(void) { return g_launches.load(); }
+
+extern "C" int noise_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.on = on != 0;
+  g_prof.recs.clear();
+  g_prof.used = 0;
+  return kStatusOk;
+}
+
+extern "C" int noise_profile_read(double* ms, int64_t* count, int kinds) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  for (int k = 0; k < kinds; ++k) ms[k] = 0.0, count[k] = 0;
+  for (const ProfRecord& r : g_prof.recs) {
+    if (r.kind < 0 || r.kind >= kinds) continue;
+    if (cudaEventSynchronize(r.b) != cudaSuccess) return kStatusLaunchFailed;
+    float t = 0.f;
+    cudaEventElapsedTime(&t, r.a, r.b);
+    ms[r.kind] += t;
+    count[r.kind] += 1;
+  }
+  return kStatusOk;
+}

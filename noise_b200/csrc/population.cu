@@ -210,6 +210,7 @@ int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& 
   }
   AttnParams ap{ctx, w.y, w.ystats, layer, layer_window(layer), status};
   dim3 grid(ctx.T / kAttnTile, kHeads, (unsigned)(rows / ctx.T));
+  LaunchScope scope(kKindAttention, stream);
   attention_window_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tm, ap);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
@@ -223,6 +224,7 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
   int rc;
   {
     EmbedParams ep{ctx, wte, lambdas, w.x, w.xb, w.inv0, w.st_a};
+    LaunchScope scope(kKindEmbed, stream);
     embed_kernel<<<(unsigned)(rows / kEmbedRows), 256, 0, stream>>>(ep);
     if (cudaGetLastError() != cudaSuccess) return kStatusLaunchFailed;
   }
@@ -230,28 +232,31 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     const __nv_bfloat16* wl = packed + l * kPackLayer;
     EpiQkv::Params q{ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
     if ((rc = launch_gemm_tc<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
-                                                  q, status, stream)))
+                                                  q, status, stream, kKindQkv)))
       return rc;
     if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
     EpiProj::Params pp{ctx, w.x, w.xb, w.ystats, w.st_b, l};
     if ((rc = launch_gemm_tc<EpiProj, kGemmStages>(w.y, wl + kPackProj, (int)rows, kWidth, kWidth, kWidth, kWidth, pp,
-                                                   status, stream)))
+                                                   status, stream, kKindProj)))
       return rc;
     EpiFc::Params fp{ctx, w.hidden, w.st_b, w.hstats, l};
     if ((rc = launch_gemm_tc<EpiFc, kGemmStages>(w.xb, wl + kPackFc, (int)rows, kHidden, kWidth, kWidth, kWidth, fp,
-                                                 status, stream)))
+                                                 status, stream, kKindFc)))
       return rc;
     const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
     EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next, l};
     if ((rc = launch_gemm_tc<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
-                                                     kHidden, mp, status, stream)))
+                                                     kHidden, mp, status, stream, kKindMlp)))
       return rc;
   }
   EpiHead::Params hp{ctx, w.st_a, w.part};
   if ((rc = launch_gemm_tc<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
-                                                 hp, status, stream)))
+                                                 hp, status, stream, kKindHead)))
     return rc;
-  member_loss_kernel<<<members, 256, 0, stream>>>(w.part, (int64_t)ctx.B * ctx.T, losses);
+  {
+    LaunchScope scope(kKindLoss, stream);
+    member_loss_kernel<<<members, 256, 0, stream>>>(w.part, (int64_t)ctx.B * ctx.T, losses);
+  }
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
 
@@ -268,6 +273,7 @@ extern "C" int64_t noise_packed_count(void) { return kPackTotal; }
 extern "C" int noise_pack_weights(const float* params, void* packed, void* stream) {
   static const PackJobs jobs = make_pack_jobs();
   dim3 grid(64, jobs.count);
+  LaunchScope scope(kKindPack, reinterpret_cast<cudaStream_t>(stream));
   pack_weights_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       params, reinterpret_cast<__nv_bfloat16*>(packed), jobs);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
