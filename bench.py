@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 EGGROLL ES update (weak-scaled over N GPUs).
+"""Benchmark of the B200 EGGROLL ES update (the 1xB200 rank-1 configuration, weak-scaled over N GPUs).
 
 One step = one full ES update: population forward of 1024 rank-1 antithetic members per GPU
 (512 directions per GPU, sigma 1e-3), every member on the same 8 Zipf(1.1) sequences x 2048 tokens,
@@ -31,9 +31,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = 'member-tokens/sec/GPU (pop 16k) and seconds per ES update at 1/2/4/8 B200'
 UNIT = 'member-tokens/s'
-PUBLISHED_PER_GPU = 2.13e6  # EGGROLL w/ Adam on 8xH100, derived member-tokens/s/GPU
+# The reference's published EGGROLL record (README.md:67: 131,072 antithetic pairs, 5.33 h for 610 updates on
+# 8xH100) is 262,144 members x 2,048 tokens per 31.5 s update: 2.13 M member-tokens/s per GPU.
+PUBLISHED_PER_GPU = 2.13e6
 SEQ, BATCH = 2048, 8
-# Algorithmic FLOPs per member-token of each kernel kind over one forward (SURVEY 8d FLOP model):
+# Algorithmic FLOPs per member-token of each kernel kind over one forward:
 # per block q,k,v,proj,fc,mlp GEMMs; attention QK+PV over visible keys only (avg keys per query
 # 768.75 for the 1024-token windows, 1024.5 for the full ones); head 512 x 4096.
 FLOPS_PER_TOKEN = {
