@@ -22,6 +22,7 @@ extern "C" {
 #define NOISE_WAIT_TIMEOUT 3
 #define NOISE_WORKSPACE_TOO_SMALL 4
 #define NOISE_UNSUPPORTED 5
+#define NOISE_SCRATCH_LIMIT 6 /* problem larger than a static scratch array holds */
 
 /* Engine self-test, no reference counterpart: C[M,N] = alpha * A[M,K] * B[N,K]^T with bf16 A and B
  * (row-major, K contiguous), fp32 accumulation, C stored as bf16 (out_bf16 != 0) or fp32.
@@ -79,6 +80,18 @@ int noise_update_sum_fe_adamw(float* params, void* packed, float* exp_avg, float
                               int pairs, float grad_scale, uint32_t seed, uint32_t step, const float* lr_mult,
                               float lr, float beta1, float beta2, float eps, float weight_decay, int adam_t,
                               float* grad_out, void* stream);
+
+/* No counterpart in the reference: noise_fitness for callers that cannot allocate device memory
+ * (an FFI host with no device allocator of its own, or a process whose device memory another
+ * allocator's pool has fully reserved). Same arguments, kernels and results as noise_fitness, but
+ * the scratch is a 2 MiB static __device__ array inside the library instead of a caller buffer.
+ * Limit: members <= noise_fitness_static_max_members() (262,144); larger calls return
+ * NOISE_SCRATCH_LIMIT. The first call on a device looks up the array's address (make it before any
+ * stream capture). All calls share the array: calls that overlap on the GPU race, so serialise them
+ * on one stream. */
+int noise_fitness_static_max_members(void);
+int noise_fitness_static(const float* losses, int members, int pairs, int mode, float* weights, int32_t* ranks,
+                         void* stream);
 
 /* Instrumentation, no reference counterpart: total kernel launches made by this library so far;
  * optional per-kind device timing with CUDA events recorded on the launching stream (kinds: 0 embed,

@@ -14,6 +14,7 @@ NOISE_OK = 0
 STATUS_NAMES = {
     0: 'ok', 1: 'bad argument', 2: 'launch failed', 3: 'device wait timed out',
     4: 'workspace too small', 5: 'unsupported configuration',
+    6: 'larger than the static scratch array holds',
 }
 
 c_void_p, c_int, c_float, c_int64, c_uint32, c_size_t, c_uint64 = (
@@ -36,6 +37,8 @@ SIGNATURES: dict[str, tuple] = {
     'noise_update_sum_fe_adamw': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_uint32,
                                           c_uint32, c_void_p, c_float, c_float, c_float, c_float, c_float, c_int,
                                           c_void_p, c_void_p]),
+    'noise_fitness_static_max_members': (c_int, []),
+    'noise_fitness_static': (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     'noise_launch_count': (c_int64, []),
     'noise_profile_enable': (c_int, [c_int]),
     'noise_profile_read': (c_int, [c_void_p, c_void_p, c_int]),
