@@ -33,7 +33,7 @@ def workspace_bytes(rows: int) -> int:
 
 def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, member_begin: int, members: int,
                       pairs: int, sigma: float, seed: int, step: int, out: torch.Tensor | None = None,
-                      status: torch.Tensor | None = None, max_workspace: int = DEFAULT_WORKSPACE_BYTES) -> torch.Tensor:
+                      status: torch.Tensor | None = None, max_workspace: int | None = None) -> torch.Tensor:
     """Mean CE of members [member_begin, member_begin + members) on every row of tokens/targets [B, T]."""
     if tokens.dim() == 1:
         tokens, targets = tokens[None], targets[None]
@@ -44,6 +44,8 @@ def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, m
     if out is None:
         out = torch.empty(members, dtype=torch.float32, device=dev)
     rows_per_member = B * T
+    if max_workspace is None:
+        max_workspace = DEFAULT_WORKSPACE_BYTES
     per_chunk = max(1, min(members, max_workspace // max(1, workspace_bytes(rows_per_member))))
     ws = workspace(dev, workspace_bytes(rows_per_member * per_chunk))
     own_status = status is None
