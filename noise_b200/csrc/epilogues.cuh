@@ -8,11 +8,14 @@
 // that the *producer* of x computed as a side statistic, so the GEMM itself is the plain shared-weight
 // product. a_m is regenerated from the counter-based stream into per-warp shared memory.
 //
-// Row statistics travel between kernels as two partial sums per row, `float [rows][2][16]`:
-//   stats for a QKV / head input x:  [0] sum x^2, [1..3] x.b_q, x.b_k, x.b_v (or [1] x.b_head),
-//                                     [4] x[:32].b_gate, [5..12] x[:32].W_gate^T (value-embedding layers)
-//   stats for an FC input x:         [0] sum x^2, [1] x.b_fc
+// Row statistics travel between kernels as partial sums (the consumer adds the parts):
+//   stats_a (QKV / head input x), float [rows][4][16]:
+//       [0] sum x^2, [1..3] x.b_q, x.b_k, x.b_v (or [1] x.b_head),
+//       [4] x[:32].b_gate, [5..12] x[:32].W_gate^T (value-embedding blocks)
+//   stats_b (FC input x), float [rows][2][2]: sum x^2, x.b_fc
+//   hstats (MLP-out input), float [rows][2]: hidden.b_mlp
 // Dot products use the bf16 values the next GEMM reads; sums of squares use the fp32 stream.
+// Every row segment moves through 32-byte (full-sector) per-thread loads and stores.
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -20,13 +23,31 @@
 
 namespace noise {
 
-constexpr int kStatStride = 16;  // floats per partial
+constexpr int kStatStride = 16;  // floats per stats_a part
+constexpr int kStatParts = 4;    // stats_a parts per row
 
 __device__ __forceinline__ float rms_scale(float ssq, int n) { return rsqrtf(ssq / (float)n + kNormEps); }
 
 // Per-warp vector slots in the epilogue's shared memory.
-constexpr int kWarpVecs = 6;
-constexpr int kEpiVecBytes = 8 * kWarpVecs * 128 * 4;
+template <int kVecs>
+struct WarpVecs {
+  static constexpr int kBytes = 8 * kVecs * 128 * 4;
+};
+
+// Sum the kStatParts parts of a stats_a row into out[0..15].
+__device__ __forceinline__ void load_stats_a(const float* stats, int64_t row, float (&out)[16]) {
+  const float* s = stats + (size_t)row * kStatParts * kStatStride;
+  ld_global_v8f(s, *reinterpret_cast<float(*)[8]>(&out[0]));
+  ld_global_v8f(s + 8, *reinterpret_cast<float(*)[8]>(&out[8]));
+#pragma unroll
+  for (int p = 1; p < kStatParts; ++p) {
+    float a[8], b[8];
+    ld_global_v8f(s + p * kStatStride, a);
+    ld_global_v8f(s + p * kStatStride + 8, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] += a[i], out[8 + i] += b[i];
+  }
+}
 
 // ---------------------------------------------------------------------------------------------
 // QKV: q, k through RoPE and a per-head RMS norm; v plus the gated value embedding.
@@ -35,12 +56,13 @@ struct EpiQkv {
   struct Params {
     PopCtx ctx;
     __nv_bfloat16* qkv;     // [rows, 1536]
-    const float* stats;     // [rows][2][16]
+    const float* stats;     // stats_a
     const float* rope;      // [T][64]: cos[0..31] | sin[0..31]
     const float* ve_table;  // [4096, 512] or nullptr
     int layer;
   };
-  static constexpr int kSmemBytes = kEpiVecBytes;
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes;
+  static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // this warp's slots: [0] a of the tile's tensor, [1] b_ve
   int lane;
@@ -48,23 +70,22 @@ struct EpiQkv {
   float inv, xb[3], gate[kHeads], a_ve_tok;
 
   __device__ EpiQkv(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * kWarpVecs * 128), lane(lane_) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_) {}
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
-    const float* s0 = p.stats + (size_t)row * 2 * kStatStride;
-    const float* s1 = s0 + kStatStride;
-    inv = rms_scale(s0[0] + s1[0], kWidth);
+    float st[16];
+    load_stats_a(p.stats, row, st);
+    inv = rms_scale(st[0], kWidth);
 #pragma unroll
-    for (int i = 0; i < 3; ++i) xb[i] = s0[1 + i] + s1[1 + i];
+    for (int i = 0; i < 3; ++i) xb[i] = st[1 + i];
     if (has_ve(p.layer)) {
-      const float xg = s0[4] + s1[4];
       const float4 ag0 = gauss4(p.ctx.key, 0, tid_gate(p.layer), 0, ri.direction);
       const float4 ag1 = gauss4(p.ctx.key, 1, tid_gate(p.layer), 0, ri.direction);
       const float ag[8] = {ag0.x, ag0.y, ag0.z, ag0.w, ag1.x, ag1.y, ag1.z, ag1.w};
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) {
-        const float pre = inv * (s0[5 + h] + s1[5 + h] + ri.sign * xg * ag[h]);
+        const float pre = inv * (st[5 + h] + ri.sign * st[4] * ag[h]);
         gate[h] = 2.0f / (1.0f + expf(-pre));
       }
       a_ve_tok = gauss1(p.ctx.key, ri.tok, tid_ve(p.layer), 0, ri.direction);
@@ -86,26 +107,24 @@ struct EpiQkv {
     const int which = col / kWidth, local = col % kWidth, head = local / kHeadDim;
     const float* a = vec + (local & 127);
     const float c2 = ri.sign * xb[which];
-    __nv_bfloat16* out = p.qkv + (size_t)row * (3 * kWidth) + col;
 #pragma unroll
     for (int j = 0; j < 64; ++j) v[j] = inv * (v[j] + c2 * a[j]);
     if (which < 2) {
-      const float4* cs = reinterpret_cast<const float4*>(p.rope + (size_t)ri.t * 64);
-      float cr[32], sr[32];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 c4 = __ldg(cs + j), s4 = __ldg(cs + 8 + j);
-        cr[4 * j] = c4.x, cr[4 * j + 1] = c4.y, cr[4 * j + 2] = c4.z, cr[4 * j + 3] = c4.w;
-        sr[4 * j] = s4.x, sr[4 * j + 1] = s4.y, sr[4 * j + 2] = s4.z, sr[4 * j + 3] = s4.w;
-      }
+      const float* cs = p.rope + (size_t)ri.t * 64;
       float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float c = cr[j], s = sr[j];
-        const float x1 = v[j], x2 = v[j + 32];
-        v[j] = x1 * c + x2 * s;
-        v[j + 32] = x2 * c - x1 * s;
-        ss += v[j] * v[j] + v[j + 32] * v[j + 32];
+      for (int j0 = 0; j0 < 32; j0 += 8) {
+        float c[8], s[8];
+        ld_global_nc_v8f(cs + j0, c);
+        ld_global_nc_v8f(cs + 32 + j0, s);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          const float x1 = v[j], x2 = v[j + 32];
+          v[j] = x1 * c[u] + x2 * s[u];
+          v[j + 32] = x2 * c[u] - x1 * s[u];
+          ss += v[j] * v[j] + v[j + 32] * v[j + 32];
+        }
       }
       const float r = rms_scale(ss, kHeadDim);
 #pragma unroll
@@ -115,21 +134,17 @@ struct EpiQkv {
       const float* bve = vec + 128 + (local & 127);
       const float g = gate[head], sa = ri.sign * a_ve_tok;
 #pragma unroll
-      for (int j = 0; j < 64; j += 4) {
-        const float4 e = __ldg(reinterpret_cast<const float4*>(ve + j));
-        v[j] += g * (e.x + sa * bve[j]);
-        v[j + 1] += g * (e.y + sa * bve[j + 1]);
-        v[j + 2] += g * (e.z + sa * bve[j + 2]);
-        v[j + 3] += g * (e.w + sa * bve[j + 3]);
+      for (int j = 0; j < 64; j += 8) {
+        float e[8];
+        ld_global_nc_v8f(ve + j, e);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[j + u] += g * (e[u] + sa * bve[j + u]);
       }
     }
-#pragma unroll
-    for (int j = 0; j < 64; j += 8)
-      st_global_v4(out + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                   pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+    st_bf16x64(p.qkv + (size_t)row * (3 * kWidth) + col, v);
   }
 
-  __device__ void end_mtile(int, int) {}
+  __device__ void end_mtile(int, int, int) {}
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -141,10 +156,11 @@ struct EpiProj {
     float* x;                // [rows, 512] fp32 residual stream, updated in place
     __nv_bfloat16* xb;       // [rows, 512] bf16 copy for the FC GEMM
     const float* ystats;     // [rows][8] per-head y.b_proj from the attention kernel
-    float* stats_out;        // [rows][2][16]: sum x^2, x.b_fc
+    float* stats_out;        // stats_b
     int layer;
   };
-  static constexpr int kSmemBytes = kEpiVecBytes;
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes;
+  static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // [0] a_proj, [1] b_fc
   int lane, half;
@@ -152,13 +168,13 @@ struct EpiProj {
   float c2, ssq, dfc;
 
   __device__ EpiProj(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * kWarpVecs * 128), lane(lane_), half(ew >> 2) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {}
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
-    const float4* ys = reinterpret_cast<const float4*>(p.ystats + (size_t)row * kHeads);
-    const float4 y0 = ys[0], y1 = ys[1];
-    c2 = ri.sign * (y0.x + y0.y + y0.z + y0.w + y1.x + y1.y + y1.z + y1.w);
+    float ys[8];
+    ld_global_v8f(p.ystats + (size_t)row * kHeads, ys);
+    c2 = ri.sign * (ys[0] + ys[1] + ys[2] + ys[3] + ys[4] + ys[5] + ys[6] + ys[7]);
     ssq = 0.f;
     dfc = 0.f;
   }
@@ -174,38 +190,29 @@ struct EpiProj {
   __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
     const float* b = vec + 128 + (col & 127);
-    float* __restrict__ xr = p.x + (size_t)row * kWidth + col;
-    __nv_bfloat16* __restrict__ xo = p.xb + (size_t)row * kWidth + col;
-    // all loads of the row segment first, so they are in flight together
-    float4 x4[16];
+    float* xr = p.x + (size_t)row * kWidth + col;
+    {
+      float x8[8][8];  // all loads of the row segment in flight together
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x4[j] = reinterpret_cast<const float4*>(xr)[j];
+      for (int j = 0; j < 8; ++j) ld_global_v8f(xr + 8 * j, x8[j]);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      v[4 * j] += x4[j].x + c2 * a[4 * j];
-      v[4 * j + 1] += x4[j].y + c2 * a[4 * j + 1];
-      v[4 * j + 2] += x4[j].z + c2 * a[4 * j + 2];
-      v[4 * j + 3] += x4[j].w + c2 * a[4 * j + 3];
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[8 * j + u] += x8[j][u] + c2 * a[8 * j + u];
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      reinterpret_cast<float4*>(xr)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    for (int j = 0; j < 64; j += 8) st_global_v8f(xr + j, v + j);
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
       ssq += v[j] * v[j];
       v[j] = bf16_round(v[j]);
       dfc += v[j] * b[j];
     }
-#pragma unroll
-    for (int j = 0; j < 64; j += 8)
-      st_global_v4(xo + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                   pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+    st_bf16x64(p.xb + (size_t)row * kWidth + col, v);
   }
 
-  __device__ void end_mtile(int, int row) {
-    float* s = p.stats_out + ((size_t)row * 2 + half) * kStatStride;
-    s[0] = ssq;
-    s[1] = dfc;
+  __device__ void end_mtile(int, int, int row) {
+    *reinterpret_cast<float2*>(p.stats_out + ((size_t)row * 2 + half) * 2) = make_float2(ssq, dfc);
   }
 };
 
@@ -216,11 +223,12 @@ struct EpiFc {
   struct Params {
     PopCtx ctx;
     __nv_bfloat16* hidden;  // [rows, 2048]
-    const float* stats;     // [rows][2][16] from EpiProj
+    const float* stats;     // stats_b
     float* hstats;          // [rows][2] partial hidden.b_mlp
     int layer;
   };
-  static constexpr int kSmemBytes = kEpiVecBytes;
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes;
+  static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // [0] a_fc, [1] b_mlp
   int lane, half;
@@ -228,14 +236,13 @@ struct EpiFc {
   float inv, c2, dmp;
 
   __device__ EpiFc(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * kWarpVecs * 128), lane(lane_), half(ew >> 2) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {}
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
-    const float* s0 = p.stats + (size_t)row * 2 * kStatStride;
-    const float* s1 = s0 + kStatStride;
-    inv = rms_scale(s0[0] + s1[0], kWidth);
-    c2 = ri.sign * (s0[1] + s1[1]);
+    const float4 s = *reinterpret_cast<const float4*>(p.stats + (size_t)row * 4);
+    inv = rms_scale(s.x + s.z, kWidth);
+    c2 = ri.sign * (s.y + s.w);
     dmp = 0.f;
   }
 
@@ -250,7 +257,6 @@ struct EpiFc {
   __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
     const float* b = vec + 128 + (col & 127);
-    __nv_bfloat16* out = p.hidden + (size_t)row * kHidden + col;
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
       const float pre = inv * (v[j] + c2 * a[j]);
@@ -258,18 +264,16 @@ struct EpiFc {
       v[j] = bf16_round(r * r);
       dmp += v[j] * b[j];
     }
-#pragma unroll
-    for (int j = 0; j < 64; j += 8)
-      st_global_v4(out + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                   pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+    st_bf16x64(p.hidden + (size_t)row * kHidden + col, v);
   }
 
-  __device__ void end_mtile(int, int row) { p.hstats[(size_t)row * 2 + half] = dmp; }
+  __device__ void end_mtile(int, int, int row) { p.hstats[(size_t)row * 2 + half] = dmp; }
 };
 
 // ---------------------------------------------------------------------------------------------
 // MLP out + residual, then the next block's x0 mixing (utils/model.py:199) and its input stats;
-// after the last block, the head's input and stats.
+// after the last block, the head's input and stats. N-interleaved schedule: the two CTAs of an
+// M tile run together so the 512 KiB hidden tile is read from DRAM once.
 // ---------------------------------------------------------------------------------------------
 struct EpiMlpOut {
   struct Params {
@@ -277,14 +281,15 @@ struct EpiMlpOut {
     float* x;               // [rows, 512] residual stream, in place
     __nv_bfloat16* xb;      // [rows, 512] next GEMM's operand
     const float* hstats;    // [rows][2]
-    float* stats_out;       // [rows][2][16]
+    float* stats_out;       // stats_a
     const float* wte;       // [4096, 512] fp32 token embedding (x0 recomputation)
     const float* inv0;      // [rows] 1/rms of the perturbed embedding row
     const float* lambdas;   // resid_lambdas[8] | x0_lambdas[8]
     const float* wgate_next;  // [8, 32] fp32 of the next block, or nullptr
     int layer;
   };
-  static constexpr int kSmemBytes = kEpiVecBytes;
+  static constexpr int kSmemBytes = WarpVecs<6>::kBytes;
+  static constexpr bool kInterleaveN = true;
   const Params& p;
   float* vec;  // [0] a_mlp, [1] b_wte, [2..4] next b_q, b_k, b_v (or [2] b_head), [5] next b_gate
   int lane, half;
@@ -293,12 +298,13 @@ struct EpiMlpOut {
   float c2, lr, l0, sa_wte, i0, ssq, d[3], dg, gp[kHeads];
 
   __device__ EpiMlpOut(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * kWarpVecs * 128), lane(lane_), half(ew >> 2),
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 6 * 128), lane(lane_), half(ew >> 2),
         last(p_.layer == kLayers - 1) {}
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
-    c2 = ri.sign * (p.hstats[(size_t)row * 2] + p.hstats[(size_t)row * 2 + 1]);
+    const float2 h = *reinterpret_cast<const float2*>(p.hstats + (size_t)row * 2);
+    c2 = ri.sign * (h.x + h.y);
     ssq = 0.f, d[0] = d[1] = d[2] = 0.f, dg = 0.f;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) gp[h] = 0.f;
@@ -333,45 +339,39 @@ struct EpiMlpOut {
   __device__ void group(int row, int col, float (&v)[64]) {
     const int c = col & 127;
     const float* a = vec + c;
-    float* __restrict__ xr = p.x + (size_t)row * kWidth + col;
-    __nv_bfloat16* __restrict__ xo = p.xb + (size_t)row * kWidth + col;
-    {
-      float4 x4[16];
+    float* xr = p.x + (size_t)row * kWidth + col;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) x4[j] = reinterpret_cast<const float4*>(xr)[j];
+    for (int h = 0; h < 64; h += 32) {  // two 32-column halves keep fewer loads live
+      float x8[4][8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        v[4 * j] += x4[j].x + c2 * a[4 * j];
-        v[4 * j + 1] += x4[j].y + c2 * a[4 * j + 1];
-        v[4 * j + 2] += x4[j].z + c2 * a[4 * j + 2];
-        v[4 * j + 3] += x4[j].w + c2 * a[4 * j + 3];
-      }
+      for (int j = 0; j < 4; ++j) ld_global_v8f(xr + h + 8 * j, x8[j]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[h + 8 * j + u] += x8[j][u] + c2 * a[h + 8 * j + u];
     }
     if (!last) {
       const float* bw = vec + 128 + c;
       const float* bq = vec + 256 + c;
       const float* bk = vec + 384 + c;
       const float* bv = vec + 512 + c;
-      const float* __restrict__ e = p.wte + (size_t)ri.tok * kWidth + col;
+      const float* e = p.wte + (size_t)ri.tok * kWidth + col;
 #pragma unroll
       for (int h = 0; h < 64; h += 32) {
-        float4 e4[8];
+        float e8[4][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) e4[j] = __ldg(reinterpret_cast<const float4*>(e + h) + j);
+        for (int j = 0; j < 4; ++j) ld_global_nc_v8f(e + h + 8 * j, e8[j]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float ev[4] = {e4[j].x, e4[j].y, e4[j].z, e4[j].w};
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int k = h + 4 * j + u;
-            const float x0 = (ev[u] + sa_wte * bw[k]) * i0;
+          for (int u = 0; u < 8; ++u) {
+            const int k = h + 8 * j + u;
+            const float x0 = (e8[j][u] + sa_wte * bw[k]) * i0;
             v[k] = lr * v[k] + l0 * x0;
           }
-        }
       }
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        reinterpret_cast<float4*>(xr)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int j = 0; j < 64; j += 8) st_global_v8f(xr + j, v + j);
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
         ssq += v[j] * v[j];
@@ -399,21 +399,15 @@ struct EpiMlpOut {
         d[0] += v[j] * bh[j];
       }
     }
-#pragma unroll
-    for (int j = 0; j < 64; j += 8)
-      st_global_v4(xo + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                   pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+    st_bf16x64(p.xb + (size_t)row * kWidth + col, v);
   }
 
-  __device__ void end_mtile(int, int row) {
-    float* s = p.stats_out + ((size_t)row * 2 + half) * kStatStride;
-    s[0] = ssq;
-    s[1] = d[0];
-    s[2] = d[1];
-    s[3] = d[2];
-    s[4] = dg;
-#pragma unroll
-    for (int h = 0; h < kHeads; ++h) s[5 + h] = gp[h];
+  __device__ void end_mtile(int, int n, int row) {
+    float* s = p.stats_out + ((size_t)row * kStatParts + 2 * n + half) * kStatStride;
+    const float w0[8] = {ssq, d[0], d[1], d[2], dg, gp[0], gp[1], gp[2]};
+    const float w1[8] = {gp[3], gp[4], gp[5], gp[6], gp[7], 0.f, 0.f, 0.f};
+    st_global_v8f(s, w0);
+    st_global_v8f(s + 8, w1);
   }
 };
 
@@ -424,10 +418,11 @@ struct EpiMlpOut {
 struct EpiHead {
   struct Params {
     PopCtx ctx;
-    const float* stats;  // [rows][2][16]: sum x^2, x.b_head
+    const float* stats;  // stats_a: sum x^2, x.b_head
     float* part;         // [rows][2][2]: sum exp(z - 15), z[target] (0 if not in this half)
   };
-  static constexpr int kSmemBytes = kEpiVecBytes;
+  static constexpr int kSmemBytes = WarpVecs<1>::kBytes;
+  static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;
   int lane, half;
@@ -435,14 +430,14 @@ struct EpiHead {
   float inv, c2, se, zt;
 
   __device__ EpiHead(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * kWarpVecs * 128), lane(lane_), half(ew >> 2) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 128), lane(lane_), half(ew >> 2) {}
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
-    const float* s0 = p.stats + (size_t)row * 2 * kStatStride;
-    const float* s1 = s0 + kStatStride;
-    inv = rms_scale(s0[0] + s1[0], kWidth);
-    c2 = ri.sign * (s0[1] + s1[1]);
+    float st[16];
+    load_stats_a(p.stats, row, st);
+    inv = rms_scale(st[0], kWidth);
+    c2 = ri.sign * st[1];
     se = 0.f;
     zt = 0.f;
   }
@@ -465,10 +460,8 @@ struct EpiHead {
     }
   }
 
-  __device__ void end_mtile(int, int row) {
-    float* o = p.part + ((size_t)row * 2 + half) * 2;
-    o[0] = se;
-    o[1] = zt;
+  __device__ void end_mtile(int, int, int row) {
+    *reinterpret_cast<float2*>(p.part + ((size_t)row * 2 + half) * 2) = make_float2(se, zt);
   }
 };
 

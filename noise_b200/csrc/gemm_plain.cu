@@ -14,11 +14,12 @@ struct EpiStore {
     int out_bf16;
   };
   static constexpr int kSmemBytes = 0;
+  static constexpr bool kInterleaveN = false;
   const Params& p;
   __device__ EpiStore(const Params& p_, uint8_t*, int, int) : p(p_) {}
   __device__ void begin_mtile(int, int) {}
   __device__ void begin_tile(int, int, int) {}
-  __device__ void end_mtile(int, int) {}
+  __device__ void end_mtile(int, int, int) {}
   __device__ void group(int row, int col, float (&v)[64]) {
     if (p.out_bf16) {
       __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col;

@@ -8,16 +8,21 @@
 //               accumulators (2 x 256 fp32 columns = all 512 columns), commits stage releases.
 //   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4).. of column half (w-2)/4 and hands 64-column
 //               groups to the epilogue functor, then releases the accumulator.
-// A CTA owns whole M tiles (all N tiles of an M tile run back to back on the same CTA), so per-row
-// state can live in epilogue registers across the N loop and A stays hot in L2 while N advances.
+// Tile schedule, chosen per epilogue (Epi::kInterleaveN):
+//   false  a CTA owns whole M tiles: all N tiles of an M tile run back to back on one CTA, so per-row
+//          state can live in epilogue registers across the N loop and A stays hot in L2;
+//   true   tiles t = m * n_tiles + n are dealt round-robin, so the n_tiles CTAs that share an A tile
+//          run at the same time and the A tile is read from DRAM once (for large-K, few-N GEMMs).
+// A "unit" is one M tile (false) or one tile (true); row state is set up per unit.
 //
 // Epilogue functor contract (all methods run on every epilogue thread; `row` is global):
 //   static constexpr int kSmemBytes;                 shared memory the functor needs
+//   static constexpr bool kInterleaveN;              tile schedule above
 //   __device__ Epi(const Params&, uint8_t* smem, int epi_warp, int lane)
-//   __device__ void begin_mtile(int m_tile, int row)
+//   __device__ void begin_mtile(int m_tile, int row)               once per unit
 //   __device__ void begin_tile(int m_tile, int n_tile, int col0)   warp-uniform; may __syncwarp
 //   __device__ void group(int row, int col, float (&v)[64])        64 consecutive columns of `row`
-//   __device__ void end_mtile(int m_tile, int row)
+//   __device__ void end_mtile(int m_tile, int n_tile, int row)     once per unit (n_tile = last one)
 #pragma once
 
 #include "profile.cuh"
@@ -29,6 +34,24 @@ struct GemmShape {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
   int* status;
+};
+
+// The tiles of one schedule unit (see the header comment).
+template <bool kInterleaveN>
+struct TileUnit {
+  int m, n_begin, n_end;
+  __device__ __forceinline__ TileUnit(int u, const GemmShape& s) {
+    if (kInterleaveN) {
+      m = u / s.n_tiles;
+      n_begin = u % s.n_tiles;
+      n_end = n_begin + 1;
+    } else {
+      m = u;
+      n_begin = 0;
+      n_end = s.n_tiles;
+    }
+  }
+  __host__ __device__ static int count(const GemmShape& s) { return kInterleaveN ? s.m_tiles * s.n_tiles : s.m_tiles; }
 };
 
 template <int kStages>
@@ -98,8 +121,11 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       for (int s = 0; s < kStages; ++s) issued[s] = false, issued_phase[s] = 0;
       const uint64_t keep = l2_policy_evict_last();  // weights: every CTA re-reads them
       bool ok = true;
-      for (int m = blockIdx.x; ok && m < shape.m_tiles; m += gridDim.x) {
-        for (int n = 0; ok && n < shape.n_tiles; ++n) {
+      const int units = TileUnit<Epi::kInterleaveN>::count(shape);
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const TileUnit<Epi::kInterleaveN> tu(u, shape);
+        const int m = tu.m;
+        for (int n = tu.n_begin; ok && n < tu.n_end; ++n) {
           for (int kb = 0; kb < shape.k_blocks; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status)) {
               ok = false;
@@ -124,8 +150,10 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       const uint32_t idesc = make_idesc(1, L::BM, L::BN);
       uint32_t stage = 0, phase = 0, t = 0;
       bool ok = true;
-      for (int m = blockIdx.x; ok && m < shape.m_tiles; m += gridDim.x) {
-        for (int n = 0; ok && n < shape.n_tiles; ++n, ++t) {
+      const int units = TileUnit<Epi::kInterleaveN>::count(shape);
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const TileUnit<Epi::kInterleaveN> tu(u, shape);
+        for (int n = tu.n_begin; ok && n < tu.n_end; ++n, ++t) {
           const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;
           if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status)) {
             ok = false;
@@ -163,10 +191,13 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
     Epi epi(ep, epi_smem, ew, lane);
     uint32_t t = 0;
     bool ok = true;
-    for (int m = blockIdx.x; ok && m < shape.m_tiles; m += gridDim.x) {
+    const int units = TileUnit<Epi::kInterleaveN>::count(shape);
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      const TileUnit<Epi::kInterleaveN> tu(u, shape);
+      const int m = tu.m;
       const int row = m * L::BM + quarter * 32 + lane;
       epi.begin_mtile(m, row);
-      for (int n = 0; n < shape.n_tiles; ++n, ++t) {
+      for (int n = tu.n_begin; n < tu.n_end; ++n, ++t) {
         const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status)) {
           ok = false;
@@ -179,8 +210,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
 #pragma unroll 1
         for (int g = 0; g < L::BN / 2 / 64; ++g) {
           float v[64];
-          tmem_ld32(taddr + g * 64, *reinterpret_cast<float(*)[32]>(&v[0]));
-          tmem_ld32(taddr + g * 64 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+          tmem_ld64(taddr + g * 64, v);
           if (g == L::BN / 2 / 64 - 1) {
             // All TMEM reads of this tile are done: hand the accumulator back to the MMA warp.
             tc_fence_before();
@@ -190,7 +220,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
           epi.group(row, n * L::BN + col0 + g * 64, v);
         }
       }
-      if (ok) epi.end_mtile(m, row);
+      if (ok) epi.end_mtile(m, tu.n_end - 1, row);
     }
   }
 
@@ -239,7 +269,8 @@ int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, i
   }
   int grid = device_sm_count();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
-  if (grid > shape.m_tiles) grid = shape.m_tiles;
+  const int units = Epi::kInterleaveN ? shape.m_tiles * shape.n_tiles : shape.m_tiles;
+  if (grid > units) grid = units;
   LaunchScope scope(kind, stream);
   gemm_tc_kernel<Epi, kStages><<<grid, L::kThreads, smem, stream>>>(ta, tb, shape, ep);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;

@@ -29,7 +29,7 @@ struct EmbedParams {
   float* x;
   __nv_bfloat16* xb;
   float* inv0;
-  float* stats;  // [rows][2][16]
+  float* stats;  // stats_a: [rows][4][16]
 };
 
 constexpr int kEmbedRows = 64;
@@ -88,7 +88,9 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
       dv += __shfl_xor_sync(0xffffffffu, dv, o);
     }
     const float vals[4] = {ssx, dq, dk, dv};
-    p.stats[(size_t)row * 2 * kStatStride + lane] = lane < 4 ? vals[lane] : 0.f;
+    float* st = p.stats + (size_t)row * kStatParts * kStatStride;  // part 0 holds the sums, parts 1..3 zero
+    st[lane] = lane < 4 ? vals[lane] : 0.f;
+    st[32 + lane] = 0.f;
     if (lane == 0) p.inv0[row] = i0;
   }
 }
@@ -173,7 +175,7 @@ struct PopWorkspace {
 
 // bytes per row of each buffer, in carve order
 static const size_t kRowBytes[] = {
-    kWidth * 4, kWidth * 2, 3 * kWidth * 2, kWidth * 2, kHidden * 2, 2 * kStatStride * 4, 2 * kStatStride * 4,
+    kWidth * 4, kWidth * 2, 3 * kWidth * 2, kWidth * 2, kHidden * 2, kStatParts * kStatStride * 4, 2 * 2 * 4,
     kHeads * 4, 2 * 4, 4, 4 * 4};
 
 size_t pop_workspace_bytes(int64_t rows) {
