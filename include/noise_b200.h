@@ -51,7 +51,7 @@ size_t noise_pop_workspace_bytes(int64_t rows);
  * s_j * (a_d b_d^T) (rank-1 factors for matrices and embeddings, eps_d for the mixing scalars) with
  * d = (j mod 2*pairs) / 2 and s_j = +sigma for even j, -sigma for odd j (:134-146). Draw d is
  * regenerated from the Philox stream keyed by (seed, step). Every member evaluates all B rows of
- * tokens/targets ([B, T] int32, T % 64 == 0, B*T % 128 == 0) and losses[j - member_begin] receives
+ * tokens/targets ([B, T] int32, T % 128 == 0) and losses[j - member_begin] receives
  * its mean next-token cross-entropy over B*T tokens. rope: [T][64] fp32 = bf16-rounded cos | sin
  * (utils/model.py:177-183). Members are processed in chunks that fit `workspace`. */
 int noise_pop_forward_lowrank(const float* params, const void* packed, const float* rope, const int32_t* tokens,

@@ -1,0 +1,275 @@
+// Sliding-window causal attention on the 5th-generation tensor cores (utils/model.py:17-31, 81-97):
+// query s sees keys s - window .. s, softmax scale 1/sqrt(64), q and k already RoPE'd and
+// RMS-normalised per head by the QKV epilogue.
+//
+// One CTA = G consecutive 128-query tiles x one head x one (member, sequence) row block. The G tiles
+// share every K/V tile the CTA streams. Warps:
+//   warp 0       TMA producer: the G Q tiles once, then 64-key K and V tiles into a 3-stage ring
+//   warp 1       TMEM owner and MMA issuer (one thread), per key tile j and query tile g:
+//                  S_g  = Q_g K_j^T    tcgen05.mma M=128 N=64 K=64, A and B K-major
+//                  O_g += P_g V_j      tcgen05.mma M=128 N=64 K=64, A = P_g (K-major smem), B = V (MN-major)
+//   warps 2..    softmax group g = 4 warps, one query row per thread: S_g from TMEM -> p = exp(s/8 - 8)
+//                (masked) -> bf16 P_g in a 128-byte-swizzled smem tile; at the end O_g / sum(p) -> y, y.b_proj.
+// The groups run out of phase with each other, so the single MMA thread keeps the tensor core busy
+// while the special-function unit works through the exponentials.
+// Because q and k are unit-RMS, |q.k| / 8 <= 8 (up to bf16 rounding), so the softmax uses the fixed
+// offset 8: no running maximum and no rescaling of the TMEM accumulator. 32-key chunks outside a
+// warp's rows' windows skip their exponentials. TMEM: group g uses S at 128g and O at 128g + 64.
+// Every wait is bounded (status word on timeout).
+#pragma once
+
+#include "model_layout.cuh"
+#include "ptx.cuh"
+
+namespace noise {
+
+struct AttnTcParams {
+  PopCtx ctx;
+  __nv_bfloat16* y;  // [rows, 512]
+  float* ystats;     // [rows][8]
+  int layer, window;
+  int* status;
+};
+
+constexpr int kAtQ = 128, kAtK = 64, kAtStages = 3;
+constexpr int kAtTileBytes = kAtK * kHeadDim * 2;  // 8 KB: 64 rows x 128 B
+constexpr int kAtQBytes = kAtQ * kHeadDim * 2;     // 16 KB
+constexpr int kAtPBytes = kAtQ * kAtK * 2;         // 16 KB
+
+template <int G>
+struct AttnTcLayout {
+  static constexpr int kThreads = (2 + 4 * G) * 32;
+  static constexpr int kCore = G * kAtQBytes + 2 * kAtStages * kAtTileBytes + G * kAtPBytes;
+  static constexpr int kSmem = 1024 + kCore + 512 + kHeadDim * 4;
+  static constexpr uint32_t kTmemCols = 128 * G;
+};
+
+template <int G>
+__global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G == 4 ? 112 : 168)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ AttnTcParams p) {
+  using L = AttnTcLayout<G>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base;                              // [g] 16 KB
+  uint8_t* sK = sQ + G * kAtQBytes;                // [stage] 8 KB
+  uint8_t* sV = sK + kAtStages * kAtTileBytes;     // [stage] 8 KB
+  uint8_t* sP = sV + kAtStages * kAtTileBytes;     // [g] 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kCore);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = q_full + 1;            // [kAtStages]
+  uint64_t* kv_empty = kv_full + kAtStages;  // [kAtStages]
+  uint64_t* s_full = kv_empty + kAtStages;   // [G]
+  uint64_t* s_empty = s_full + G;            // [G]
+  uint64_t* p_full = s_empty + G;            // [G]
+  uint64_t* p_empty = p_full + G;            // [G]
+  uint64_t* o_full = p_empty + G;
+  uint64_t* drain = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* bproj = reinterpret_cast<float*>(base + L::kCore + 512);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.ctx.T;
+  const int n_units = T / (kAtQ * G);
+  const int unit = n_units - 1 - blockIdx.x;  // longest key ranges first
+  const int head = blockIdx.y;
+  const int64_t row_base = (int64_t)blockIdx.z * T;
+  const int q0 = unit * kAtQ * G;  // first query of the CTA
+  const int kt_begin = max(0, q0 - p.window) / kAtK;
+  const int kt_end = (q0 + kAtQ * G - 1) / kAtK;
+  const int n_kt = kt_end - kt_begin + 1;
+  int* status = p.status;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kAtStages; ++s) mbar_init(&kv_full[s], 1), mbar_init(&kv_empty[s], 1);
+    for (int g = 0; g < G; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&s_empty[g], 4);
+      mbar_init(&p_full[g], 4);
+      mbar_init(&p_empty[g], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tensormap(&tm_qkv);
+  }
+  if (tid >= 64 && tid < 80) {  // the member's c_proj column factor for this head's 64 columns
+    const RowInfo r0 = row_info(p.ctx, row_base);
+    reinterpret_cast<float4*>(bproj)[tid - 64] =
+        gauss4(p.ctx.key, (head * kHeadDim >> 2) + (tid - 64), tid_proj(p.layer), 1, r0.direction);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int qcol = head * kHeadDim, kcol = kWidth + head * kHeadDim, vcol = 2 * kWidth + head * kHeadDim;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      mbar_arrive_expect_tx(q_full, G * kAtQBytes);
+      for (int b = 0; b < 2 * G; ++b)
+        tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_qkv, q_full, qcol, (int)(row_base + q0 + 64 * b));
+      int issued = 0;
+      for (int j = 0; j < n_kt; ++j) {
+        const int st = j % kAtStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, status)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kAtTileBytes);
+        const int r = (int)(row_base + (kt_begin + j) * kAtK);
+        tma_load_2d(sK + st * kAtTileBytes, &tm_qkv, &kv_full[st], kcol, r);
+        tma_load_2d(sV + st * kAtTileBytes, &tm_qkv, &kv_full[st], vcol, r);
+        issued = j + 1;
+      }
+      // copies in flight land before the CTA can exit
+      mbar_wait(q_full, 0, abort_flag, status);
+      for (int j = max(0, issued - kAtStages); j < issued; ++j)
+        mbar_wait(&kv_full[j % kAtStages], (j / kAtStages) & 1, abort_flag, status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc_s = make_idesc(1, kAtQ, kAtK);
+      const uint32_t idesc_o = make_idesc(1, kAtQ, kHeadDim, 0, 1);  // B = V is MN-major
+      bool ok = mbar_wait(q_full, 0, abort_flag, status);
+      tc_fence_after();
+      for (int j = 0; ok && j <= n_kt; ++j) {
+        if (j < n_kt) {
+          const int st = j % kAtStages;
+          if (!mbar_wait(&kv_full[st], (j / kAtStages) & 1, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t dk = smem_desc_sw128(sK + st * kAtTileBytes);
+          for (int g = 0; g < G && ok; ++g) {
+            if (!mbar_wait(&s_empty[g], (j & 1) ^ 1, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t dq = smem_desc_sw128(sQ + g * kAtQBytes);
+#pragma unroll
+            for (int k = 0; k < kHeadDim / 16; ++k)
+              tc_mma_f16(tmem + 128 * g, dq + 2 * k, dk + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+            tc_commit(&s_full[g]);
+          }
+        }
+        if (ok && j > 0) {
+          const int jj = j - 1, st = jj % kAtStages;
+          const uint64_t dv = smem_desc_sw128_mn(sV + st * kAtTileBytes);
+          for (int g = 0; g < G && ok; ++g) {
+            if (!mbar_wait(&p_full[g], jj & 1, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t dp = smem_desc_sw128(sP + g * kAtPBytes);
+#pragma unroll
+            for (int k = 0; k < kAtK / 16; ++k)
+              tc_mma_f16(tmem + 128 * g + 64, dp + 2 * k, dv + (uint64_t)(2048 >> 4) * k, idesc_o,
+                         (jj > 0 || k > 0) ? 1u : 0u);
+            tc_commit(&p_empty[g]);
+          }
+          if (ok) tc_commit(&kv_empty[st]);
+        }
+      }
+      if (ok) tc_commit(o_full);
+      tc_commit(drain);
+      mbar_wait(drain, 0, abort_flag, status);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax + output ----------------
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;      // row of query tile g = TMEM lane
+    const int qg = q0 + kAtQ * g;           // first query of tile g
+    const int q = qg + r;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + 128 * g, tO = tS + 64;
+    const float kScaleLog2 = 0.125f * 1.4426950408889634f;
+    const float kOffsetLog2 = 8.0f * 1.4426950408889634f;
+    float lsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+    bool ok = true;
+    uint8_t* prow = sP + g * kAtPBytes + r * 128;
+    const int qlo = qg + quarter * 32, qhi = qlo + 31;  // this warp's rows
+    for (int j = 0; j < n_kt; ++j) {
+      const int k0 = (kt_begin + j) * kAtK;
+      if (!mbar_wait(&s_full[g], j & 1, abort_flag, status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[64];
+      tmem_ld64(tS + lane_addr, sv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[g]);
+      if (!mbar_wait(&p_empty[g], (j & 1) ^ 1, abort_flag, status)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int kc = k0 + 32 * c;
+        // warp-uniform classification of the 32 x 32 block (this warp's rows x the chunk's keys)
+        const bool none = kc > qhi || qlo - (kc + 31) > p.window;
+        const bool all = (kc + 31 <= qlo) && (qhi - kc <= p.window);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {  // 8 keys = one 16-byte chunk of the P row
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+          if (!none) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = 32 * c + 8 * b + 2 * u;
+              float e0 = ex2_approx(sv[i] * kScaleLog2 - kOffsetLog2);
+              float e1 = ex2_approx(sv[i + 1] * kScaleLog2 - kOffsetLog2);
+              if (!all) {
+                const int key = kc + 8 * b + 2 * u;
+                if (key > q || q - key > p.window) e0 = 0.f;
+                if (key + 1 > q || q - key - 1 > p.window) e1 = 0.f;
+              }
+              lsum[u] += e0 + e1;
+              w[u] = pack_bf16x2(e0, e1);
+            }
+          }
+          // P row r: chunk (4c + b) stored at (4c + b) ^ (r % 8) (128-byte swizzle)
+          *reinterpret_cast<uint4*>(prow + (((4 * c + b) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[g]);
+    }
+    if (ok && mbar_wait(o_full, 0, abort_flag, status)) {
+      tc_fence_after();
+      float o[64];
+      tmem_ld64(tO + lane_addr, o);
+      const float inv = 1.0f / ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
+      float d = 0.f;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        o[j] = bf16_round(o[j] * inv);
+        d += o[j] * bproj[j];
+      }
+      st_bf16x64(p.y + (row_base + q) * kWidth + head * kHeadDim, o);
+      p.ystats[(row_base + q) * kHeads + head] = d;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+}  // namespace noise

@@ -13,7 +13,7 @@
 //   member loss      mean over the member's B*T rows
 // No noise tensor is ever materialised: every kernel regenerates its draws from (seed, step,
 // direction, tensor).
-#include "attention.cuh"
+#include "attention_tc.cuh"
 #include "epilogues.cuh"
 #include "noise_b200.h"
 
@@ -198,23 +198,32 @@ PopWorkspace carve(void* ws, int64_t rows) {
 
 constexpr int kGemmStages = 4;
 
-int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& w, int64_t rows, int layer,
-                     int* status, cudaStream_t stream) {
-  CUtensorMap tm;
-  if (make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, kAttnTile, kHeadDim))
-    return kStatusBadArgument;
+template <int G>
+int launch_attention_g(const CUtensorMap& tm, const AttnTcParams& ap, int64_t rows, cudaStream_t stream) {
+  using L = AttnTcLayout<G>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attention_window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem) !=
+    if (cudaFuncSetAttribute(attention_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
         cudaSuccess)
       return kStatusLaunchFailed;
     configured = true;
   }
-  AttnParams ap{ctx, w.y, w.ystats, layer, layer_window(layer), status};
-  dim3 grid(ctx.T / kAttnTile, kHeads, (unsigned)(rows / ctx.T));
+  dim3 grid(ap.ctx.T / (kAtQ * G), kHeads, (unsigned)(rows / ap.ctx.T));
   LaunchScope scope(kKindAttention, stream);
-  attention_window_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tm, ap);
+  attention_tc_kernel<G><<<grid, L::kThreads, L::kSmem, stream>>>(tm, ap);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& w, int64_t rows, int layer,
+                     int* status, cudaStream_t stream) {
+  CUtensorMap tm;
+  if (make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, 64, kHeadDim))
+    return kStatusBadArgument;
+  AttnTcParams ap{ctx, w.y, w.ystats, layer, layer_window(layer), status};
+  const int n_qt = ctx.T / kAtQ;  // query tiles per sequence; a CTA takes 4, 2 or 1 of them
+  if (n_qt % 4 == 0) return launch_attention_g<4>(tm, ap, rows, stream);
+  if (n_qt % 2 == 0) return launch_attention_g<2>(tm, ap, rows, stream);
+  return launch_attention_g<1>(tm, ap, rows, stream);
 }
 
 int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const float* rope, const PopCtx& ctx,
@@ -287,7 +296,7 @@ extern "C" int noise_pop_forward_lowrank(const float* params, const void* packed
                                          uint32_t step, float* losses, void* workspace, size_t workspace_bytes,
                                          int* status, void* stream) {
   if (!params || !packed || !rope || !tokens || !targets || !losses || !workspace) return kStatusBadArgument;
-  if (B <= 0 || T <= 0 || T % kAttnTile || ((int64_t)B * T) % 128 || members <= 0 || pairs <= 0 ||
+  if (B <= 0 || T <= 0 || T % kAtQ || ((int64_t)B * T) % 128 || members <= 0 || pairs <= 0 ||
       member_begin < 0 || T > 20480)
     return kStatusBadArgument;
   const int64_t rows_per_member = (int64_t)B * T;

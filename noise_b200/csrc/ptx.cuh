@@ -66,6 +66,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `ns` nanoseconds (it resumes as soon
+// as the phase completes), so waiting warps do not spin on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait on a phase parity. Returns false when the cycle budget ran out or when another role
 // of the same CTA raised `abort` (a shared flag); in the first case the global status is set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
@@ -73,8 +87,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if ((it & 15u) == 0) {
       if (*abort) return false;
       if (clock64() - start > kWaitCycleBudget) {
         *abort = 1;
@@ -212,11 +226,27 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major operand tile written by TMA with 128-byte swizzle:
+// 128-byte rows along K, N (or M) contiguous inside a row, 8-row groups 1024 bytes apart. The
+// leading byte offset (stride between 64-element MN blocks) is set equal to the stride byte offset
+// so every address the unit can form stays inside the tile when MN spans one block.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)(1024 >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor: fp32 accumulator, A/B of the given format (0 = f16, 1 = bf16; 2 = tf32
-// under kind::tf32), both K-major, M x N tile.
-__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, int M, int N) {
-  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
+// under kind::tf32), M x N tile; a_mn / b_mn select MN-major (transposed) operands.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, int M, int N, uint32_t a_mn = 0,
+                                                  uint32_t b_mn = 0) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (a_mn << 15) | (b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Load 32 consecutive fp32 columns of this warp's 32 TMEM lanes (one row per thread), without
@@ -261,6 +291,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 2^x on the special-function unit (one MUFU.EX2, flush-to-zero; ~2 ulp)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
