@@ -120,28 +120,42 @@ class Eggroll:
     def evaluate(self, x: torch.Tensor, y: torch.Tensor, step: int) -> torch.Tensor:
         """This rank's member losses [members / world] (device)."""
         members = self.members(len(x))
-        per_rank = members // self.world
-        begin = self.rank * per_rank
+        begin, end = self.member_range(len(x))
+        per_rank = end - begin
         if self.all_sequences:
             noise = CounterNoise(begin, per_rank, self.pairs, self.sigma, self.seed, step)
             return self.loss(self.model, None, noise, None, x, y)
         per_seq = members // len(x)
         losses = torch.empty(per_rank, device=self.device)
-        for start in range(begin, begin + per_rank, 2 * self.chunk):
+        start = begin
+        while start < end:  # blocks of up to 2 * chunk members, never straddling two sequences
             seq = start // per_seq
-            count = min(2 * self.chunk, begin + per_rank - start, (seq + 1) * per_seq - start)
+            count = min(2 * self.chunk, end - start, (seq + 1) * per_seq - start)
             noise = CounterNoise(start, count, self.pairs, self.sigma, self.seed, step)
             losses[start - begin:start - begin + count] = self.loss(self.model, None, noise, None, x[seq], y[seq])
+            start += count
         return losses
+
+    def member_range(self, batch: int) -> tuple[int, int]:
+        """[begin, end) of the members this rank evaluates (train/val/eggroll.py:134-139)."""
+        members = self.members(batch)
+        if members % self.world:
+            raise ValueError(f'{members} members do not split over {self.world} ranks')
+        per_rank = members // self.world
+        return self.rank * per_rank, (self.rank + 1) * per_rank
+
+    def gather(self, losses: torch.Tensor) -> torch.Tensor:
+        """All ranks' member losses in member order (train/val/eggroll.py:147-150)."""
+        if self.world == 1:
+            return losses
+        gathered = [torch.empty_like(losses) for _ in range(self.world)]
+        torch.distributed.all_gather(gathered, losses)
+        return torch.cat(gathered)
 
     @torch.no_grad()
     def step(self, x, y, optimizer: AdamW, step: int) -> float:
         """Evaluate this rank's share of the population, gather the losses, rebuild the update everywhere."""
-        losses = self.evaluate(x, y, step)
-        if self.world > 1:
-            gathered = [torch.empty_like(losses) for _ in range(self.world)]
-            torch.distributed.all_gather(gathered, losses)
-            losses = torch.cat(gathered)
+        losses = self.gather(self.evaluate(x, y, step))
         self.last_losses = losses
         w = fitness_weights(losses, self.pairs, self.fitness)
         optimizer.zero_grad(set_to_none=True)
