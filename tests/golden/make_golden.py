@@ -11,6 +11,11 @@ on CPU in float32 and saves their outputs as small .npz fixtures beside this scr
                    CHUNK = 1, two sequences of T = 384, step 1 -> member losses, the gradients handed
                    to AdamW (full for small tensors, checksums and sampled entries for matrices) and
                    the parameter change after AdamW.
+  dust.npz         train/val/run.py DUST pieces on two sequences of T = 128: orthogonal_noise with
+                   injected frames and signs, coordinate_differences, reward_to_go, and
+                   direct_errors (real capture + rerun + centring + contraction) for a writers group,
+                   an MLP hidden site (live-unit mask), the embedding (rerun from the embedding) and
+                   an attention-output hub with reward-to-go, each with its reassembled gradient.
 
 Only the attention primitive is swapped, for the mathematically identical masked SDPA
 (`(q >= k) & (q - k <= window)`), because torch.compile(flex_attention) does not lower on CPU here;
@@ -60,8 +65,12 @@ def sample_entries(t: torch.Tensor, n: int = 64, seed: int = 0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', type=Path, required=True)
+    ap.add_argument('--only-dust', action='store_true')
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
+    if args.only_dust:
+        dust_golden(args.reference)
+        raise SystemExit
     import utils.model as um
     import train.val.eggroll as eg
     um.attention = sdpa_window
@@ -142,5 +151,83 @@ def main():
     print('eggroll step', mean_loss, torch.cat(seen_losses).tolist())
 
 
+def dust_golden(reference):
+    """DUST fixtures; only orthogonal_noise's random frames and signs are injected."""
+    from oracle import dust as od
+    torch._dynamo.config.disable = True
+    import train.val.run as run
+    run.attention = sdpa_window
+    torch.manual_seed(0)
+    model = run.make_model(torch.device('cpu'), SEED)
+    est = run.DUST(model, run.recipe(0.01), SEED, 0, 1)
+    rows = zipf_tokens(2, 129, seed=4)
+    x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+    y[1, 5] = -1  # an ignored target
+    est.capture(x, y)
+    b, t = x.shape
+    out = dict(tokens=rows.numpy().astype(np.int16), targets=y.numpy().astype(np.int64),
+               clean_loss=est.clean_loss.numpy())
+
+    def inject(site, draws, chunk, n, b_, t_, d, dtype=None):
+        sid = od.site_id(site)
+        total = draws  # world 1
+        cycles = -(-total // d)
+        pats, offs = od.frame(SEED, STEP, sid, cycles, d, b_, t_)
+        idx = chunk * n + np.arange(n)
+        signs = od.draw_signs(SEED, STEP, sid, idx, b_, t_)
+        est.frames[site] = (pats, offs)
+        orig = est.signs
+        est.signs = lambda *shape, shared=False: signs[..., None] if shape == (n, b_, t_, 1) else orig(*shape, shared=shared)
+        try:
+            a = run.DUST.orthogonal_noise(est, site, draws, chunk, n, b_, t_, d, dtype)
+        finally:
+            est.signs = orig
+        return a
+
+    # orthogonal_noise itself
+    a = inject('transformer.h.1.mlp.c_fc', 96, 1, 16, b, t, 2048)
+    out['ortho_fc'] = a.numpy().astype(np.int8)
+    est.frames.clear()
+    # coordinate differences and reward-to-go
+    g = torch.Generator().manual_seed(9)
+    raw = torch.randn(2, 16, 4096, generator=g) * 3
+    tg = torch.randint(0, 4096, (2, 16), generator=g)
+    tg[0, 3] = -1
+    out['cd_raw'], out['cd_targets'] = raw.numpy(), tg.numpy()
+    out['cd'] = run.coordinate_differences(raw, tg, 0.1).numpy()
+    rw = torch.randn(3, 2, 40, generator=g)
+    out['rtg_in'], out['rtg'] = rw.numpy(), run.reward_to_go(rw, 0.3).numpy()
+    # direct errors through the reference's own reruns
+    est.orthogonal_noise = lambda site, draws, chunk, n, b_, t_, d, dtype=None: inject(site, draws, chunk, n, b_, t_, d, dtype)
+    cases = [
+        ('writers', ['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj'], 32, 0.4, 1, 0.0),
+        ('hidden', ['transformer.h.6.mlp.c_fc'], 16, 0.4, 6, 0.0),
+        ('embed', ['transformer.wte'], 16, 0.8, None, 0.0),
+        ('hub', ['o@0'], 16, 0.4, 0, 0.3),
+    ]
+    for name, sites, draws, sigma, entry, gamma in cases:
+        est.frames.clear()
+        errs = est.direct_errors(sites, draws, sigma, entry, gamma, {})
+        for k, site in enumerate(sites):
+            out[f'de_{name}_{k}'] = errs[site].numpy()
+            if not site.startswith('o@'):
+                out[f'ra_{name}_{k}'] = est.reassemble(site, errs[site]).numpy()
+        out[f'de_{name}_meta'] = np.array([draws, sigma, -1 if entry is None else entry, gamma])
+    packed = {}
+    for k, v in out.items():
+        v = np.asarray(v)
+        if v.size > 8192:  # large arrays: checksums + 4096 sampled entries keep the fixture small
+            t_ = torch.from_numpy(v.astype(np.float64))
+            idx, vals = sample_entries(t_, n=4096, seed=len(k))
+            packed[k + '__sums'] = checksums(t_)
+            packed[k + '__idx'], packed[k + '__val'] = idx, vals
+            packed[k + '__shape'] = np.array(v.shape)
+        else:
+            packed[k] = v
+    np.savez_compressed(HERE / 'dust.npz', **packed)
+    print('dust', {k: v.shape for k, v in out.items() if k.startswith('de_')})
+
+
 if __name__ == '__main__':
     main()
+    dust_golden(None)
