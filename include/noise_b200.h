@@ -59,6 +59,63 @@ int noise_pop_forward_lowrank(const float* params, const void* packed, const flo
                               float sigma, uint32_t seed, uint32_t step, float* losses, void* workspace,
                               size_t workspace_bytes, int* status, void* stream);
 
+/* Direct-draw rerun of DUST (train/val/run.py:256-279 DUST.rerun with orthogonal_noise :223-238).
+ * Sites (bit k of mask): 0 'transformer.wte' (entry must be -1: rerun from the embedding),
+ * 1 'o' (attention output), 2 'attn' (attn.c_proj output), 3 'fc' (mlp.c_fc pre-activation, live
+ * units only), 4 'mlp' (mlp.c_proj output). site[k] is the stream id of site k's draws (the
+ * parameter tensor id whose output is jittered; hubs o@i use 64 + i; the embedding uses 2). */
+typedef struct NoiseDirect {
+  int entry;            /* first block rerun, -1 = from the embedding */
+  uint32_t mask;        /* sites jittered in block `entry` */
+  uint32_t site[5];
+  float sigma;          /* jitter scale (draws are +-1) */
+  const float* x_entry; /* [B*T, 512] clean input of block `entry` (entry >= 0) */
+  const float* inv0;    /* [B*T] clean 1/rms of the embedding rows (entry >= 0) */
+  const void* live;     /* bf16 [B*T, 2048] clean relu^2 hidden of block `entry` (fc site) */
+} NoiseDirect;
+
+/* Replaces DUST.rerun (train/val/run.py:256-279) for draws [draw_begin, draw_begin + draws) of the
+ * sites in spec: weights unperturbed, draw i adds sigma * a_i (orthogonal draws regenerated from the
+ * (seed, step) stream) at its sites in block `entry`, every draw evaluates all B rows, and
+ * token_loss[i - draw_begin][b][t] receives the per-token cross-entropy (0 where targets < 0). */
+int noise_pop_forward_direct(const float* params, const void* packed, const float* rope, const int32_t* tokens,
+                             const int32_t* targets, int B, int T, int64_t draw_begin, int draws,
+                             const NoiseDirect* spec, uint32_t seed, uint32_t step, float* token_loss, void* workspace,
+                             size_t workspace_bytes, int* status, void* stream);
+
+/* Clean forward of the unperturbed model keeping what DUST's reruns and reassembly need
+ * (train/val/run.py:189-209 hooks, capture :244-254). All arrays are caller-owned, rows = B*T. */
+typedef struct NoiseCapture {
+  float* blocks;      /* [8][rows][512] block inputs after the x0 mixing */
+  float* x0;          /* [rows][512] normalised embedding */
+  float* inv0;        /* [rows] 1/rms of the embedding rows */
+  void* y;            /* bf16 [8][rows][512] attention outputs (c_proj inputs) */
+  float* mid;         /* [8][rows][512] residual stream after the attention */
+  void* hidden;       /* bf16 [8][rows][2048] relu^2 hidden (mlp.c_proj inputs) */
+  float* final_x;     /* [rows][512] residual stream after the last block */
+  float* logits;      /* [rows][4096] raw logits before the soft cap */
+  float* token_loss;  /* [rows] per-token cross-entropy (0 where targets < 0) */
+} NoiseCapture;
+
+int noise_pop_capture(const float* params, const void* packed, const float* rope, const int32_t* tokens,
+                      const int32_t* targets, int B, int T, const NoiseCapture* out, void* workspace,
+                      size_t workspace_bytes, int* status, void* stream);
+
+/* Replaces the contraction of DUST.direct_errors (train/val/run.py:347-368, without the memory
+ * prior) for one site: with perturbed [draws][B*T] from noise_pop_forward_direct and clean [B*T],
+ * rewards clean - perturbed are centred over chunks of `chunk` consecutive draws, optionally turned
+ * into reward-to-go with decay gamma (run.py:81-86), and errors [B*T][d] -= sum_i reward_i a_i / sigma,
+ * masked by live (bf16 [B*T][d] > 0) when given. draws <= 2048 per call; the caller divides by the
+ * site's total draw count. */
+int noise_dust_errors(const float* clean, const float* perturbed, int draws, int chunk, int B, int T,
+                      int64_t draw_begin, uint32_t site, int d, float sigma, float gamma, const void* live,
+                      uint32_t seed, uint32_t step, float* errors, void* stream);
+
+/* Replaces coordinate_differences (train/val/run.py:120-137): raw logits [rows][4096] -> the central
+ * difference of each token's soft-capped CE along each of its logits, zero where targets < 0. */
+int noise_coordinate_differences(const float* raw, const int32_t* targets, int64_t rows, float sigma, float* out,
+                                 void* stream);
+
 /* Scratch bytes noise_fitness needs for `members` losses. */
 size_t noise_fitness_workspace_bytes(int members);
 

@@ -32,6 +32,14 @@ SIGNATURES: dict[str, tuple] = {
     'noise_pop_forward_lowrank': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int64,
                                           c_int, c_int, c_float, c_uint32, c_uint32, c_void_p, c_void_p, c_size_t,
                                           c_void_p, c_void_p]),
+    'noise_pop_forward_direct': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int64,
+                                         c_int, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_size_t, c_void_p,
+                                         c_void_p]),
+    'noise_pop_capture': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                                  c_void_p, c_size_t, c_void_p, c_void_p]),
+    'noise_dust_errors': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_uint32, c_int, c_float,
+                                  c_float, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+    'noise_coordinate_differences': (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p, c_void_p]),
     'noise_fitness_workspace_bytes': (c_size_t, [c_int]),
     'noise_fitness': (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     'noise_update_sum_fe_adamw': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_uint32,
@@ -47,6 +55,18 @@ SIGNATURES: dict[str, tuple] = {
 
 class NoiseError(RuntimeError):
     pass
+
+
+class NoiseDirect(ctypes.Structure):
+    """struct NoiseDirect of include/noise_b200.h."""
+    _fields_ = [('entry', ctypes.c_int), ('mask', ctypes.c_uint32), ('site', ctypes.c_uint32 * 5),
+                ('sigma', ctypes.c_float), ('x_entry', c_void_p), ('inv0', c_void_p), ('live', c_void_p)]
+
+
+class NoiseCapture(ctypes.Structure):
+    """struct NoiseCapture of include/noise_b200.h."""
+    _fields_ = [(n, c_void_p) for n in ('blocks', 'x0', 'inv0', 'y', 'mid', 'hidden', 'final_x', 'logits',
+                                         'token_loss')]
 
 
 _lib = None

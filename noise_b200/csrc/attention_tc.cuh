@@ -253,10 +253,16 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
       float o[64];
       tmem_ld64(tO + lane_addr, o);
       const float inv = 1.0f / ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
+      // direct mode: the draw added to the attention output (site 'o', before c_proj)
+      const SiteJitter jit = site_jitter(p.ctx, p.layer, kSiteO, row_base + q, kWidth);
+      uint32_t patw[4] = {0u, 0u, 0u, 0u};
+      if (jit.on) site_patterns(p.ctx, kSiteO, jit.r, (head * kHeadDim) & ~127, patw);
       float d = 0.f;
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
-        o[j] = bf16_round(o[j] * inv);
+        const int col = head * kHeadDim + j;
+        const float jv = jit.on ? jit.scale * draw_value(jit.r, col, patw[(col & 127) >> 5]) : 0.f;
+        o[j] = bf16_round(o[j] * inv + jv);
         d += o[j] * bproj[j];
       }
       st_bf16x64(p.y + (row_base + q) * kWidth + head * kHeadDim, o);

@@ -166,6 +166,8 @@ struct EpiProj {
   int lane, half;
   RowInfo ri;
   float c2, ssq, dfc;
+  SiteJitter jit;  // direct mode: draw added to the c_proj output (site 'attn')
+  uint32_t patw[4];
 
   __device__ EpiProj(const Params& p_, uint8_t* smem, int ew, int lane_)
       : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {}
@@ -177,6 +179,7 @@ struct EpiProj {
     c2 = ri.sign * (ys[0] + ys[1] + ys[2] + ys[3] + ys[4] + ys[5] + ys[6] + ys[7]);
     ssq = 0.f;
     dfc = 0.f;
+    jit = site_jitter(p.ctx, p.layer, kSiteAttn, row, kWidth);
   }
 
   __device__ void begin_tile(int m_tile, int, int col0) {
@@ -185,11 +188,17 @@ struct EpiProj {
     warp_gauss128(vec, p.ctx.key, tid_proj(p.layer), 0, r0.direction, col0, lane);
     warp_gauss128(vec + 128, p.ctx.key, tid_fc(p.layer), 1, r0.direction, col0, lane);
     __syncwarp();
+    if (jit.on) site_patterns(p.ctx, kSiteAttn, jit.r, col0, patw);
   }
 
   __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
     const float* b = vec + 128 + (col & 127);
+    if (jit.on) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
+    }
     float* xr = p.x + (size_t)row * kWidth + col;
     {
       float x8[8][8];  // all loads of the row segment in flight together
@@ -234,6 +243,8 @@ struct EpiFc {
   int lane, half;
   RowInfo ri;
   float inv, c2, dmp;
+  SiteJitter jit;  // direct mode: draw added to the live units' pre-activation (site 'fc')
+  uint32_t patw[4];
 
   __device__ EpiFc(const Params& p_, uint8_t* smem, int ew, int lane_)
       : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {}
@@ -244,6 +255,7 @@ struct EpiFc {
     inv = rms_scale(s.x + s.z, kWidth);
     c2 = ri.sign * (s.y + s.w);
     dmp = 0.f;
+    jit = site_jitter(p.ctx, p.layer, kSiteFc, row, kHidden);
   }
 
   __device__ void begin_tile(int m_tile, int, int col0) {
@@ -252,14 +264,25 @@ struct EpiFc {
     warp_gauss128(vec, p.ctx.key, tid_fc(p.layer), 0, r0.direction, col0, lane);
     warp_gauss128(vec + 128, p.ctx.key, tid_mlp(p.layer), 1, r0.direction, col0, lane);
     __syncwarp();
+    if (jit.on) site_patterns(p.ctx, kSiteFc, jit.r, col0, patw);
   }
 
   __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
     const float* b = vec + 128 + (col & 127);
 #pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = inv * (v[j] + c2 * a[j]);
+    if (jit.on) {
+      const int64_t seq_rows = (int64_t)p.ctx.B * p.ctx.T;
+      const __nv_bfloat16* lv = p.ctx.dir.live + (size_t)(row % seq_rows) * kHidden + col;
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (__bfloat162float(lv[j]) > 0.f)
+          v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
+    }
+#pragma unroll
     for (int j = 0; j < 64; ++j) {
-      const float pre = inv * (v[j] + c2 * a[j]);
+      const float pre = v[j];
       const float r = fmaxf(pre, 0.f);
       v[j] = bf16_round(r * r);
       dmp += v[j] * b[j];
@@ -286,6 +309,7 @@ struct EpiMlpOut {
     const float* inv0;      // [rows] 1/rms of the perturbed embedding row
     const float* lambdas;   // resid_lambdas[8] | x0_lambdas[8]
     const float* wgate_next;  // [8, 32] fp32 of the next block, or nullptr
+    float* x_final;         // [rows, 512] fp32 output of the last block (capture only), or nullptr
     int layer;
   };
   static constexpr int kSmemBytes = WarpVecs<6>::kBytes;
@@ -296,6 +320,8 @@ struct EpiMlpOut {
   bool last;
   RowInfo ri;
   float c2, lr, l0, sa_wte, i0, ssq, d[3], dg, gp[kHeads];
+  SiteJitter jit, jit_wte;  // direct mode: site 'mlp' in this block; the embedding draw inside x0
+  uint32_t patw[4], patw_wte[4];
 
   __device__ EpiMlpOut(const Params& p_, uint8_t* smem, int ew, int lane_)
       : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 6 * 128), lane(lane_), half(ew >> 2),
@@ -315,6 +341,8 @@ struct EpiMlpOut {
       sa_wte = ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction);
       i0 = p.inv0[row];
     }
+    jit = site_jitter(p.ctx, p.layer, kSiteMlp, row, kWidth);
+    jit_wte = site_jitter(p.ctx, -1, kSiteWte, row, kWidth);  // on for every block when rerun from the embedding
   }
 
   __device__ void begin_tile(int m_tile, int, int col0) {
@@ -334,11 +362,17 @@ struct EpiMlpOut {
       warp_gauss128(vec + 256, p.ctx.key, kTidHead, 1, dir, col0, lane);
     }
     __syncwarp();
+    if (jit.on) site_patterns(p.ctx, kSiteMlp, jit.r, col0, patw);
+    if (jit_wte.on) site_patterns(p.ctx, kSiteWte, jit_wte.r, col0, patw_wte);
   }
 
   __device__ void group(int row, int col, float (&v)[64]) {
     const int c = col & 127;
     const float* a = vec + c;
+    if (jit.on) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
+    }
     float* xr = p.x + (size_t)row * kWidth + col;
 #pragma unroll
     for (int h = 0; h < 64; h += 32) {  // two 32-column halves keep fewer loads live
@@ -366,7 +400,9 @@ struct EpiMlpOut {
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int k = h + 8 * j + u;
-            const float x0 = (e8[j][u] + sa_wte * bw[k]) * i0;
+            float ek = e8[j][u] + sa_wte * bw[k];
+            if (jit_wte.on) ek += jit_wte.scale * draw_value(jit_wte.r, col + k, patw_wte[((col + k) & 127) >> 5]);
+            const float x0 = ek * i0;
             v[k] = lr * v[k] + l0 * x0;
           }
       }
@@ -392,6 +428,10 @@ struct EpiMlpOut {
       }
     } else {
       const float* bh = vec + 256 + c;
+      if (p.x_final) {
+#pragma unroll
+        for (int j = 0; j < 64; j += 8) st_global_v8f(p.x_final + (size_t)row * kWidth + col + j, v + j);
+      }
 #pragma unroll
       for (int j = 0; j < 64; ++j) {
         ssq += v[j] * v[j];
@@ -420,6 +460,7 @@ struct EpiHead {
     PopCtx ctx;
     const float* stats;  // stats_a: sum x^2, x.b_head
     float* part;         // [rows][2][2]: sum exp(z - 15), z[target] (0 if not in this half)
+    float* logits;       // [rows, 4096] raw logits before the soft cap (capture only), or nullptr
   };
   static constexpr int kSmemBytes = WarpVecs<1>::kBytes;
   static constexpr bool kInterleaveN = false;
@@ -449,8 +490,15 @@ struct EpiHead {
     __syncwarp();
   }
 
-  __device__ void group(int, int col, float (&v)[64]) {
+  __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
+    if (p.logits) {
+      float lg[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) lg[j] = inv * (v[j] + c2 * a[j]);
+#pragma unroll
+      for (int j = 0; j < 64; j += 8) st_global_v8f(p.logits + (size_t)row * kVocab + col + j, lg + j);
+    }
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
       const float logit = inv * (v[j] + c2 * a[j]);

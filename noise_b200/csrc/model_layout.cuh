@@ -8,8 +8,10 @@
 //   then lm_head (4096 x 512).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "dust.cuh"
 #include "philox.cuh"
 
 namespace noise {
@@ -83,6 +85,21 @@ constexpr int64_t kPackLayer = kPackMlp + (int64_t)kWidth * kHidden;
 constexpr int64_t kPackHead = kLayers * kPackLayer;
 constexpr int64_t kPackTotal = kPackHead + (int64_t)kVocab * kWidth;
 
+// Direct-draw (DUST rerun) mode: weights unperturbed, member j of the call is draw
+// member_begin + j, rerun from block `entry` (-1: from the embedding) with the orthogonal draws
+// of the sites in `mask` added in that block (train/val/run.py:256-279, block_forward :102-117).
+struct DirectSpec {
+  int on;
+  int entry;
+  uint32_t mask;                  // bits kSiteWte, kSiteO, kSiteAttn, kSiteFc, kSiteMlp
+  uint32_t site[kSiteKinds];      // stream site id per site kind
+  float sigma;                    // jitter scale (the draws are +-1)
+  const float* x_entry;           // [B*T, 512] clean input of block `entry` (entry >= 0)
+  const float* inv0;              // [B*T] clean 1/rms of the embedding rows (entry >= 0)
+  const __nv_bfloat16* live;      // [B*T, 2048] clean relu^2 hidden of block `entry`: > 0 marks live units
+  float* token_loss;              // [members, B, T] per-token cross-entropy
+};
+
 // Everything a kernel needs to place a row of the population batch: rows are ordered
 // (member, sequence, token), member j = member_begin + row / (B * T).
 struct PopCtx {
@@ -91,9 +108,38 @@ struct PopCtx {
   int T, B;
   int64_t member_begin;
   int pairs;           // antithetic directions P: member j uses direction (j mod 2P) / 2
-  float sigma;         // member j perturbs by +sigma (even j) or -sigma (odd j)
+  float sigma;         // member j perturbs by +sigma (even j) or -sigma (odd j); 0 in direct mode
   PhiloxKey key;
+  DirectSpec dir;
 };
+
+// Jitter of a direct-mode site in one row: the draw's Hadamard row and sign, and scale.
+struct SiteJitter {
+  bool on;
+  DrawRow r;
+  float scale;
+};
+
+__device__ __forceinline__ SiteJitter site_jitter(const PopCtx& c, int layer, uint32_t kind, int64_t row,
+                                                  uint32_t d) {
+  SiteJitter j;
+  j.on = c.dir.on && layer == c.dir.entry && ((c.dir.mask >> kind) & 1u);
+  j.scale = c.dir.sigma;
+  if (j.on) {
+    const int64_t seq_rows = (int64_t)c.B * c.T;
+    const uint32_t idx = (uint32_t)(c.member_begin + row / seq_rows);
+    j.r = draw_row(c.key, c.dir.site[kind], idx, (uint32_t)(row % seq_rows), d);
+  }
+  return j;
+}
+
+// The 4 pattern words of columns [c0, c0 + 128) (c0 % 128 == 0) for the row's draw cycle.
+__device__ __forceinline__ void site_patterns(const PopCtx& c, uint32_t kind, const DrawRow& r, uint32_t c0,
+                                              uint32_t (&w)[4]) {
+  uint32_t x[4];
+  philox4x32_10(c0 >> 7, (c.dir.site[kind] << 2) | 1u, r.cycle, kDomainDirect, c.key.k0, c.key.k1, x);
+  w[0] = x[0], w[1] = x[1], w[2] = x[2], w[3] = x[3];
+}
 
 struct RowInfo {
   uint32_t direction;

@@ -29,20 +29,28 @@ struct EmbedParams {
   float* x;
   __nv_bfloat16* xb;
   float* inv0;
-  float* stats;  // stats_a: [rows][4][16]
+  float* stats;   // stats_a: [rows][4][16]
+  float* x0_out;  // [rows, 512] normalised embedding (capture only), or nullptr
 };
 
 constexpr int kEmbedRows = 64;
 
 __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ EmbedParams p) {
   __shared__ float4 sv[4][kWidth / 4];  // b_wte, b_q0, b_k0, b_v0
+  __shared__ uint32_t patw[kWidth / 32];  // direct mode: pattern words of the embedding draw
   const int64_t row0 = (int64_t)blockIdx.x * kEmbedRows;
   const RowInfo r0 = row_info(p.ctx, row0);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int i = tid; i < 4 * (kWidth / 4); i += blockDim.x) {
     const int v = i / (kWidth / 4), blk = i % (kWidth / 4);
     const uint32_t tensor = v == 0 ? kTidWte : v == 1 ? tid_q(0) : v == 2 ? tid_k(0) : tid_v(0);
-    sv[v][blk] = gauss4(p.ctx.key, blk, tensor, 1, r0.direction);
+    sv[v][blk] = p.ctx.sigma != 0.f ? gauss4(p.ctx.key, blk, tensor, 1, r0.direction) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const SiteJitter j0 = site_jitter(p.ctx, -1, kSiteWte, row0, kWidth);  // same draw for the whole CTA
+  if (j0.on && tid < kWidth / 128) {
+    uint32_t w[4];
+    site_patterns(p.ctx, kSiteWte, j0.r, tid * 128, w);
+    for (int k = 0; k < 4; ++k) patw[tid * 4 + k] = w[k];
   }
   __syncthreads();
   const float mix = p.lambdas[0] + r0.sign * gauss1(p.ctx.key, 0, kTidResid, 0, r0.direction) + p.lambdas[kLayers] +
@@ -50,7 +58,8 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
   for (int rr = warp; rr < kEmbedRows; rr += 8) {
     const int64_t row = row0 + rr;
     const RowInfo ri = row_info(p.ctx, row);
-    const float sa = ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction);
+    const float sa = p.ctx.sigma != 0.f ? ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction) : 0.f;
+    const SiteJitter jit = site_jitter(p.ctx, -1, kSiteWte, row, kWidth);
     const float4* w = reinterpret_cast<const float4*>(p.wte + (size_t)ri.tok * kWidth);
     float4 e[4];
     float ss = 0.f;
@@ -59,6 +68,14 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
       const int c4 = lane + 32 * k;
       const float4 wv = __ldg(w + c4), bv = sv[0][c4];
       e[k] = make_float4(wv.x + sa * bv.x, wv.y + sa * bv.y, wv.z + sa * bv.z, wv.w + sa * bv.w);
+      if (jit.on) {
+        const uint32_t c = 4 * c4;
+        const uint32_t pw = patw[c >> 5];
+        e[k].x += jit.scale * draw_value(jit.r, c, pw);
+        e[k].y += jit.scale * draw_value(jit.r, c + 1, pw);
+        e[k].z += jit.scale * draw_value(jit.r, c + 2, pw);
+        e[k].w += jit.scale * draw_value(jit.r, c + 3, pw);
+      }
       ss += e[k].x * e[k].x + e[k].y * e[k].y + e[k].z * e[k].z + e[k].w * e[k].w;
     }
 #pragma unroll
@@ -70,7 +87,9 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int c4 = lane + 32 * k;
-      const float4 xi = make_float4(mix * (e[k].x * i0), mix * (e[k].y * i0), mix * (e[k].z * i0), mix * (e[k].w * i0));
+      const float4 x0v = make_float4(e[k].x * i0, e[k].y * i0, e[k].z * i0, e[k].w * i0);
+      if (p.x0_out) reinterpret_cast<float4*>(p.x0_out + (size_t)row * kWidth)[c4] = x0v;
+      const float4 xi = make_float4(mix * x0v.x, mix * x0v.y, mix * x0v.z, mix * x0v.w);
       xo[c4] = xi;
       ssx += xi.x * xi.x + xi.y * xi.y + xi.z * xi.z + xi.w * xi.w;
       const float r[4] = {bf16_round(xi.x), bf16_round(xi.y), bf16_round(xi.z), bf16_round(xi.w)};
@@ -93,6 +112,42 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
     st[32 + lane] = 0.f;
     if (lane == 0) p.inv0[row] = i0;
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// direct mode from block `entry` >= 0: every draw starts from the clean input of that block
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) direct_start_kernel(const __grid_constant__ EmbedParams p, int64_t rows) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t seq = row % ((int64_t)p.ctx.B * p.ctx.T);
+  const float4* src = reinterpret_cast<const float4*>(p.ctx.dir.x_entry + (size_t)seq * kWidth);
+  float4* xo = reinterpret_cast<float4*>(p.x + (size_t)row * kWidth);
+  uint2* xbo = reinterpret_cast<uint2*>(p.xb + (size_t)row * kWidth);
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c4 = lane + 32 * k;
+    const float4 v = __ldg(src + c4);
+    xo[c4] = v;
+    xbo[c4] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  float* st = p.stats + (size_t)row * kStatParts * kStatStride;
+  st[lane] = lane == 0 ? ss : 0.f;
+  st[32 + lane] = 0.f;
+  if (lane == 0) p.inv0[row] = p.ctx.dir.inv0[seq];
+}
+
+// per-token cross-entropy from the head's pieces; ignored targets (< 0) score 0
+__global__ void token_loss_kernel(const float* part, const int* targets, int64_t rows, int64_t seq_rows, float* out) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const float4 q = reinterpret_cast<const float4*>(part)[r];
+  out[r] = targets[r % seq_rows] < 0 ? 0.f : logf(q.x + q.z) + kSoftCap - (q.y + q.w);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -226,49 +281,97 @@ int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& 
   return launch_attention_g<1>(tm, ap, rows, stream);
 }
 
+// Optional copies of the clean forward's intermediates (one member, sigma = 0): what DUST's
+// reruns and reassembly need (train/val/run.py:189-209, :244-254).
+struct CaptureBufs {
+  float* blocks;           // [8][rows][512] block inputs after the x0 mixing
+  float* x0;               // [rows][512]
+  float* inv0;             // [rows]
+  __nv_bfloat16* y;        // [8][rows][512] attention outputs (c_proj inputs)
+  float* mid;              // [8][rows][512] residual stream after the attention (c_fc input before its norm)
+  __nv_bfloat16* hidden;   // [8][rows][2048] relu^2 hidden (mlp.c_proj inputs; > 0 marks live units)
+  float* final_x;          // [rows][512] residual stream after the last block
+  float* logits;           // [rows][4096] raw logits before the soft cap
+};
+
 int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const float* rope, const PopCtx& ctx,
-                      int members, float* losses, PopWorkspace& w, int* status, cudaStream_t stream) {
+                      int members, float* losses, PopWorkspace& w, int* status, cudaStream_t stream,
+                      const CaptureBufs* cap = nullptr) {
   static const ParamLayout L = make_param_layout();
   const int64_t rows = (int64_t)members * ctx.B * ctx.T;
   const float* wte = params + L.offset[kTidWte];
   const float* lambdas = params + L.offset[kTidResid];  // resid_lambdas then x0_lambdas, contiguous
+  const bool direct = ctx.dir.on != 0;
+  const int first = (direct && ctx.dir.entry >= 0) ? ctx.dir.entry : 0;
+  auto copy = [&](void* dst, const void* src, size_t bytes) {
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, stream) == cudaSuccess;
+  };
   int rc;
   {
-    EmbedParams ep{ctx, wte, lambdas, w.x, w.xb, w.inv0, w.st_a};
-    LaunchScope scope(kKindEmbed, stream);
-    embed_kernel<<<(unsigned)(rows / kEmbedRows), 256, 0, stream>>>(ep);
+    EmbedParams ep{ctx, wte, lambdas, w.x, w.xb, w.inv0, w.st_a, cap ? cap->x0 : nullptr};
+    if (first > 0 || (direct && ctx.dir.entry == 0)) {
+      LaunchScope scope(kKindEmbed, stream);
+      direct_start_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(ep, rows);
+    } else {
+      LaunchScope scope(kKindEmbed, stream);
+      embed_kernel<<<(unsigned)(rows / kEmbedRows), 256, 0, stream>>>(ep);
+    }
     if (cudaGetLastError() != cudaSuccess) return kStatusLaunchFailed;
+    if (cap && !(copy(cap->inv0, w.inv0, rows * 4) && copy(cap->blocks, w.x, rows * kWidth * 4)))
+      return kStatusLaunchFailed;
   }
-  for (int l = 0; l < kLayers; ++l) {
+  for (int l = first; l < kLayers; ++l) {
     const __nv_bfloat16* wl = packed + l * kPackLayer;
     EpiQkv::Params q{ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
     if ((rc = launch_gemm_tc<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
                                                   q, status, stream, kKindQkv)))
       return rc;
     if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
+    if (cap && !copy(cap->y + (size_t)l * rows * kWidth, w.y, rows * kWidth * 2)) return kStatusLaunchFailed;
     EpiProj::Params pp{ctx, w.x, w.xb, w.ystats, w.st_b, l};
     if ((rc = launch_gemm_tc<EpiProj, kGemmStages>(w.y, wl + kPackProj, (int)rows, kWidth, kWidth, kWidth, kWidth, pp,
                                                    status, stream, kKindProj)))
       return rc;
+    if (cap && !copy(cap->mid + (size_t)l * rows * kWidth, w.x, rows * kWidth * 4)) return kStatusLaunchFailed;
     EpiFc::Params fp{ctx, w.hidden, w.st_b, w.hstats, l};
     if ((rc = launch_gemm_tc<EpiFc, kGemmStages>(w.xb, wl + kPackFc, (int)rows, kHidden, kWidth, kWidth, kWidth, fp,
                                                  status, stream, kKindFc)))
       return rc;
+    if (cap && !copy(cap->hidden + (size_t)l * rows * kHidden, w.hidden, rows * kHidden * 2)) return kStatusLaunchFailed;
     const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
-    EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next, l};
+    EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next,
+                         (cap && l == kLayers - 1) ? cap->final_x : nullptr, l};
     if ((rc = launch_gemm_tc<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
                                                      kHidden, mp, status, stream, kKindMlp)))
       return rc;
+    if (cap && l + 1 < kLayers && !copy(cap->blocks + (size_t)(l + 1) * rows * kWidth, w.x, rows * kWidth * 4))
+      return kStatusLaunchFailed;
   }
-  EpiHead::Params hp{ctx, w.st_a, w.part};
+  EpiHead::Params hp{ctx, w.st_a, w.part, cap ? cap->logits : nullptr};
   if ((rc = launch_gemm_tc<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
                                                  hp, status, stream, kKindHead)))
     return rc;
   {
     LaunchScope scope(kKindLoss, stream);
-    member_loss_kernel<<<members, 256, 0, stream>>>(w.part, (int64_t)ctx.B * ctx.T, losses);
+    if (direct || cap)
+      token_loss_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
+          w.part, ctx.targets, rows, (int64_t)ctx.B * ctx.T, direct ? ctx.dir.token_loss : losses);
+    else
+      member_loss_kernel<<<members, 256, 0, stream>>>(w.part, (int64_t)ctx.B * ctx.T, losses);
   }
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+int check_pop_shape(int B, int T, int members) {
+  if (B <= 0 || T <= 0 || T % kAtQ || ((int64_t)B * T) % 128 || members <= 0 || T > 20480) return kStatusBadArgument;
+  return kStatusOk;
+}
+
+int pop_chunk_members(int64_t rows_per_member, int members, size_t workspace_bytes) {
+  int chunk = members;
+  while (chunk > 0 && pop_workspace_bytes(rows_per_member * chunk) > workspace_bytes) --chunk;
+  while (chunk > 0 && (int64_t)chunk * rows_per_member > (int64_t)1 << 30) --chunk;  // int32 GEMM row indices
+  return chunk;
 }
 
 }  // namespace noise
@@ -296,22 +399,72 @@ extern "C" int noise_pop_forward_lowrank(const float* params, const void* packed
                                          uint32_t step, float* losses, void* workspace, size_t workspace_bytes,
                                          int* status, void* stream) {
   if (!params || !packed || !rope || !tokens || !targets || !losses || !workspace) return kStatusBadArgument;
-  if (B <= 0 || T <= 0 || T % kAtQ || ((int64_t)B * T) % 128 || members <= 0 || pairs <= 0 ||
-      member_begin < 0 || T > 20480)
-    return kStatusBadArgument;
+  if (check_pop_shape(B, T, members) || pairs <= 0 || member_begin < 0) return kStatusBadArgument;
   const int64_t rows_per_member = (int64_t)B * T;
-  int chunk = members;
-  while (chunk > 0 && pop_workspace_bytes(rows_per_member * chunk) > workspace_bytes) --chunk;
+  const int chunk = pop_chunk_members(rows_per_member, members, workspace_bytes);
   if (chunk == 0) return kStatusWorkspaceTooSmall;
-  while ((int64_t)chunk * rows_per_member > (int64_t)1 << 30) --chunk;  // int32 row indices in the GEMM
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < members; m0 += chunk) {
     const int mc = members - m0 < chunk ? members - m0 : chunk;
-    PopCtx ctx{tokens, targets, T, B, member_begin + m0, pairs, sigma, PhiloxKey{seed, step}};
+    PopCtx ctx{tokens, targets, T, B, member_begin + m0, pairs, sigma, PhiloxKey{seed, step}, DirectSpec{}};
     PopWorkspace w = carve(workspace, rows_per_member * mc);
     const int rc = pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, mc,
                                      losses + m0, w, status, s);
     if (rc) return rc;
   }
   return kStatusOk;
+}
+
+extern "C" int noise_pop_forward_direct(const float* params, const void* packed, const float* rope,
+                                        const int32_t* tokens, const int32_t* targets, int B, int T,
+                                        int64_t draw_begin, int draws, const NoiseDirect* spec, uint32_t seed,
+                                        uint32_t step, float* token_loss, void* workspace, size_t workspace_bytes,
+                                        int* status, void* stream) {
+  if (!params || !packed || !rope || !tokens || !targets || !token_loss || !workspace || !spec) return kStatusBadArgument;
+  if (check_pop_shape(B, T, draws) || draw_begin < 0) return kStatusBadArgument;
+  if (spec->entry < -1 || spec->entry >= kLayers || spec->mask == 0 || (spec->mask >> kSiteKinds)) return kStatusBadArgument;
+  if (spec->entry == -1 && spec->mask != (1u << kSiteWte)) return kStatusBadArgument;
+  if (spec->entry >= 0 && ((spec->mask & 1u) || !spec->x_entry || !spec->inv0)) return kStatusBadArgument;
+  if (((spec->mask >> kSiteFc) & 1u) && !spec->live) return kStatusBadArgument;
+  const int64_t rows_per_member = (int64_t)B * T;
+  const int chunk = pop_chunk_members(rows_per_member, draws, workspace_bytes);
+  if (chunk == 0) return kStatusWorkspaceTooSmall;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int m0 = 0; m0 < draws; m0 += chunk) {
+    const int mc = draws - m0 < chunk ? draws - m0 : chunk;
+    DirectSpec d{};
+    d.on = 1;
+    d.entry = spec->entry;
+    d.mask = spec->mask;
+    for (int k = 0; k < kSiteKinds; ++k) d.site[k] = spec->site[k];
+    d.sigma = spec->sigma;
+    d.x_entry = spec->x_entry;
+    d.inv0 = spec->inv0;
+    d.live = reinterpret_cast<const __nv_bfloat16*>(spec->live);
+    d.token_loss = token_loss + m0 * rows_per_member;
+    PopCtx ctx{tokens, targets, T, B, draw_begin + m0, 1, 0.0f, PhiloxKey{seed, step}, d};
+    PopWorkspace w = carve(workspace, rows_per_member * mc);
+    const int rc = pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, mc, nullptr,
+                                     w, status, s);
+    if (rc) return rc;
+  }
+  return kStatusOk;
+}
+
+extern "C" int noise_pop_capture(const float* params, const void* packed, const float* rope, const int32_t* tokens,
+                                 const int32_t* targets, int B, int T, const NoiseCapture* out, void* workspace,
+                                 size_t workspace_bytes, int* status, void* stream) {
+  if (!params || !packed || !rope || !tokens || !targets || !out || !workspace) return kStatusBadArgument;
+  if (!out->blocks || !out->x0 || !out->inv0 || !out->y || !out->mid || !out->hidden || !out->final_x ||
+      !out->logits || !out->token_loss)
+    return kStatusBadArgument;
+  if (check_pop_shape(B, T, 1)) return kStatusBadArgument;
+  const int64_t rows = (int64_t)B * T;
+  if (pop_workspace_bytes(rows) > workspace_bytes) return kStatusWorkspaceTooSmall;
+  CaptureBufs cap{out->blocks, out->x0, out->inv0, reinterpret_cast<__nv_bfloat16*>(out->y), out->mid,
+                  reinterpret_cast<__nv_bfloat16*>(out->hidden), out->final_x, out->logits};
+  PopCtx ctx{tokens, targets, T, B, 0, 1, 0.0f, PhiloxKey{0, 0}, DirectSpec{}};
+  PopWorkspace w = carve(workspace, rows);
+  return pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, 1, out->token_loss, w,
+                           status, reinterpret_cast<cudaStream_t>(stream), &cap);
 }
