@@ -77,7 +77,8 @@ typedef struct NoiseDirect {
 /* Replaces DUST.rerun (train/val/run.py:256-279) for draws [draw_begin, draw_begin + draws) of the
  * sites in spec: weights unperturbed, draw i adds sigma * a_i (orthogonal draws regenerated from the
  * (seed, step) stream) at its sites in block `entry`, every draw evaluates all B rows, and
- * token_loss[i - draw_begin][b][t] receives the per-token cross-entropy (0 where targets < 0). */
+ * token_loss[i - draw_begin][b][t] receives the per-token cross-entropy (0 where targets < 0).
+ * entry = -1 with mask = 0 is the plain forward with per-token losses. */
 int noise_pop_forward_direct(const float* params, const void* packed, const float* rope, const int32_t* tokens,
                              const int32_t* targets, int B, int T, int64_t draw_begin, int draws,
                              const NoiseDirect* spec, uint32_t seed, uint32_t step, float* token_loss, void* workspace,
@@ -115,6 +116,25 @@ int noise_dust_errors(const float* clean, const float* perturbed, int draws, int
  * difference of each token's soft-capped CE along each of its logits, zero where targets < 0. */
 int noise_coordinate_differences(const float* raw, const int32_t* targets, int64_t rows, float sigma, float* out,
                                  void* stream);
+
+/* Replaces torch.optim.AdamW.step on dense gradients (the DUST estimator's; train/val/run.py:652-655):
+ * grad is a full flat gradient buffer; lr_per_tensor[60] gives each tensor's learning rate, < 0
+ * for tensors another optimizer owns. adam_t is the 1-based step for the bias corrections. */
+int noise_adamw_dense(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* grad,
+                      const float* lr_per_tensor, float beta1, float beta2, float eps, float weight_decay, int adam_t,
+                      void* stream);
+
+/* ANVIL II (train/val/run.py:583-626) over the 48 block matrices in named_parameters order, split
+ * around `polar` (:572-580), whose quintic maps the caller runs on x as bf16 matmuls. Buffers with
+ * the flat parameter layout: grad, fast, slow, scratch (fp32), x (bf16); energy [lanes]; partials
+ * [2 * tiles]; scalars [matrices] (sizes from noise_anvil_sizes).
+ * prepare: fast/slow EMAs, m = g.lerp(w fast + (1-w) slow, beta), x = bf16(m / (1.05 |m| + 1e-6)).
+ * finish: x holds polar(m); lane-energy EMA, normalisation, sign-gated decay, parameter update. */
+int noise_anvil_sizes(int64_t* tiles, int64_t* lanes, int* matrices);
+int noise_anvil_prepare(const float* grad, float* fast, float* slow, float* scratch, void* x, float* partials,
+                        float* scalars, float fast_beta, float slow_beta, float beta, float weight, void* stream);
+int noise_anvil_finish(float* params, void* packed, const float* slow, const void* update, float* energy,
+                       float* partials, float* scalars, float lane_beta, float lr, float weight_decay, void* stream);
 
 /* Scratch bytes noise_fitness needs for `members` losses. */
 size_t noise_fitness_workspace_bytes(int members);

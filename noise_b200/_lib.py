@@ -40,6 +40,13 @@ SIGNATURES: dict[str, tuple] = {
     'noise_dust_errors': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_uint32, c_int, c_float,
                                   c_float, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
     'noise_coordinate_differences': (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p, c_void_p]),
+    'noise_adamw_dense': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_float,
+                                  c_float, c_float, c_int, c_void_p]),
+    'noise_anvil_sizes': (c_int, [c_void_p, c_void_p, c_void_p]),
+    'noise_anvil_prepare': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float,
+                                    c_float, c_float, c_float, c_void_p]),
+    'noise_anvil_finish': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float,
+                                   c_float, c_float, c_void_p]),
     'noise_fitness_workspace_bytes': (c_size_t, [c_int]),
     'noise_fitness': (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     'noise_update_sum_fe_adamw': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_uint32,

@@ -422,8 +422,9 @@ extern "C" int noise_pop_forward_direct(const float* params, const void* packed,
                                         int* status, void* stream) {
   if (!params || !packed || !rope || !tokens || !targets || !token_loss || !workspace || !spec) return kStatusBadArgument;
   if (check_pop_shape(B, T, draws) || draw_begin < 0) return kStatusBadArgument;
-  if (spec->entry < -1 || spec->entry >= kLayers || spec->mask == 0 || (spec->mask >> kSiteKinds)) return kStatusBadArgument;
-  if (spec->entry == -1 && spec->mask != (1u << kSiteWte)) return kStatusBadArgument;
+  if (spec->entry < -1 || spec->entry >= kLayers || (spec->mask >> kSiteKinds)) return kStatusBadArgument;
+  if (spec->entry == -1 && spec->mask != (1u << kSiteWte) && spec->mask != 0) return kStatusBadArgument;
+  if (spec->entry >= 0 && spec->mask == 0) return kStatusBadArgument;
   if (spec->entry >= 0 && ((spec->mask & 1u) || !spec->x_entry || !spec->inv0)) return kStatusBadArgument;
   if (((spec->mask >> kSiteFc) & 1u) && !spec->live) return kStatusBadArgument;
   const int64_t rows_per_member = (int64_t)B * T;

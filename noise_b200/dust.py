@@ -175,3 +175,135 @@ def reassemble(cap: Capture, name: str, error: torch.Tensor) -> torch.Tensor:
     else:
         inp = cap.module_input(site(name))
     return err.t() @ inp
+
+
+# ------------------------------------------------------------------------------------------------
+# the estimator
+# ------------------------------------------------------------------------------------------------
+@dataclass
+class Recipe:
+    """Draws per update summed over GPUs, lists per block (run.py:41-59)."""
+    writers: list
+    hidden: list
+    hubs: list
+    embedding: int
+    local: dict
+    nrep: int
+    lr: float
+    betas: tuple = (0.7, 0.95)
+    warmdown: float = 0.0
+    gamma: float = 0.98
+    first_gamma: float = 0.3
+    anvil_lr: float = 0.023
+    anvil_wd: float = 2.25
+    memory_beta: float = 0.9
+    mesa_ridge: float = 0.1
+    alpha_beta: float = 0.8
+
+
+def recipe(scale: float) -> Recipe:
+    """The tuned 16k Adam cell with every draw count scaled, rounded to multiples of 64 (run.py:62-70)."""
+    count = lambda k: max(64, round(k * scale / 64) * 64)  # noqa: E731
+    return Recipe(writers=[count(256)] * LAYERS, hidden=[count(512)] * LAYERS, hubs=[count(512)] * LAYERS,
+                  embedding=count(2048),
+                  local=dict(q=count(384), v=count(384), gate=count(128), k=count(1664), ve=count(4608)),
+                  nrep=16, lr=0.003, warmdown=0.3)
+
+
+def token_losses(w: Weights, cap: Capture) -> torch.Tensor:
+    """Per-token losses [B, T] of the current (unperturbed) weights: a plain forward from the embedding."""
+    spec = _lib.NoiseDirect()
+    spec.entry, spec.mask, spec.sigma = -1, 0, 0.0
+    dev = w.device
+    out = torch.empty(cap.B, cap.T, dtype=torch.float32, device=dev)
+    ws = workspace(dev, workspace_bytes(cap.B * cap.T))
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.call('noise_pop_forward_direct', w.flat.data_ptr(), w.packed.data_ptr(), w.rope(cap.T).data_ptr(),
+              cap.x.data_ptr(), cap.y.data_ptr(), cap.B, cap.T, 0, 1, _lib.ctypes.byref(spec), 0, 0,
+              out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(), _stream(dev))
+    return out
+
+
+class DUST:
+    """Forward-only gradient estimator of train/val/run.py:162-542 on noise_b200's kernels.
+
+    Built here: capture, the coordinate head (head_error), direct errors of the writers, the MLP
+    hidden layer, the embedding and the attention-output hubs (with the first block's reward-to-go),
+    reassembly, two-sided ES on the mixing scalars, the rank average with its finite check, and the
+    ANVIL II + AdamW step. Not built yet: the attention-internal local errors (q, k, v, gate, value
+    embeddings; run.py:391-463) and the credit-memory prior (run.py:281-330); those parameters keep a
+    zero estimate."""
+
+    def __init__(self, w: Weights, rec: Recipe, seed: int = 0, rank: int = 0, world: int = 1):
+        counts = rec.writers + rec.hidden + rec.hubs + [rec.embedding] + list(rec.local.values())
+        if any(k % world for k in counts) or 8 % world:
+            raise ValueError('Every draw count must split evenly across the GPUs.')
+        self.w, self.recipe, self.seed, self.rank, self.world = w, rec, seed, rank, world
+        self.t = 0
+        self.cap = None
+
+    def _errors(self, names, count, sigma, entry=None, gamma=0.0):
+        per = count // self.world
+        return direct_errors(self.w, self.cap, names, per, sigma, entry, gamma, self.seed, self.t,
+                             draw_offset=self.rank * per, nrep=self.recipe.nrep)
+
+    def scalar_gradients(self, draws: int, sigma: float = 0.03) -> dict:
+        """Two-sided ES for the 16 mixing scalars (run.py:473-491). The Gaussian directions come from
+        a CPU generator seeded by (seed, step, rank), so every rank draws its own."""
+        dev = self.w.device
+        lam = self.w.flat[:2 * LAYERS]  # resid_lambdas | x0_lambdas, contiguous at the front
+        clean = lam.clone()
+        estimate = torch.zeros(2 * LAYERS, dtype=torch.float32, device=dev)
+        valid = (self.cap.y >= 0).float()
+        g = torch.Generator().manual_seed((self.seed * 1_000_003 + self.t) * 8 + self.rank)
+        try:
+            for _ in range(draws):
+                a = torch.randn(2 * LAYERS, generator=g).to(dev)
+                losses = []
+                for sign in (1.0, -1.0):
+                    lam.copy_(clean + sign * sigma * a)
+                    losses.append(token_losses(self.w, self.cap))
+                diff = ((losses[0] - losses[1]) * valid).sum() / (2 * sigma)
+                estimate += diff * a / draws
+        finally:
+            lam.copy_(clean)
+        return {'resid_lambdas': estimate[:LAYERS], 'x0_lambdas': estimate[LAYERS:]}
+
+    def _average(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+            t.div_(self.world)
+        return t
+
+    @torch.no_grad()
+    def step(self, x, y, optimizer) -> float:
+        from .optim import DenseGrad
+        self.t += 1
+        r, layers = self.recipe, LAYERS
+        self.cap = cap = Capture(self.w, x, y)
+        grads = DenseGrad(self.w)
+        head = head_error(cap)
+        grads.views['lm_head.weight'].copy_(reassemble(cap, 'lm_head', head))
+        for layer in range(layers):
+            pre = f'transformer.h.{layer}.'
+            gamma = r.first_gamma if layer == 0 else 0.0
+            for names, count in (([pre + 'attn.c_proj', pre + 'mlp.c_proj'], r.writers[layer]),
+                                 ([pre + 'mlp.c_fc'], r.hidden[layer])):
+                for name, err in self._errors(names, count, 0.4, layer, gamma).items():
+                    grads.views[name + '.weight'].copy_(reassemble(cap, name, err))
+        err = self._errors(['transformer.wte'], r.embedding, 0.8)['transformer.wte']
+        grads.views['transformer.wte.weight'].copy_(reassemble(cap, 'transformer.wte', err))
+        self.targets = {}
+        for layer in range(layers):
+            sigma = 0.4 if layer < layers // 2 else 0.8
+            gamma = r.first_gamma if layer == 0 else 0.0
+            self.targets[layer] = self._average(self._errors([f'o@{layer}'], r.hubs[layer], sigma, layer, gamma)[f'o@{layer}'])
+        for name, est in self.scalar_gradients(8 // self.world).items():
+            grads.views[name].copy_(est)
+        valid = (cap.y >= 0).sum().float()
+        grads.flat.div_(valid)
+        self._average(grads.flat)
+        if not torch.isfinite(grads.flat).all():
+            raise FloatingPointError('Non-finite estimate')
+        optimizer.step(grads)
+        return cap.clean_loss.view(cap.B, cap.T)[cap.y >= 0].mean().item()

@@ -1,0 +1,173 @@
+"""Optimizers for dense gradients: ANVIL II on the block matrices and AdamW elsewhere, the
+`make_optimizer` split of train/val/run.py:629-656, on noise_b200's kernels.
+
+ANVIL's elementwise and reduction passes run in noise_anvil_prepare / noise_anvil_finish, batched
+over all 48 block matrices; its six quintic maps (`polar`, run.py:572-580) run between them as
+batched bf16 matmuls in the reference's operation order. Tall matrices (c_fc, 2048 x 512) are
+orthogonalised through their right Gram matrix, y <- a y + y (b S + (c S) S) with S = y^T y, which
+equals polar applied to the transpose.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .model import PARAM_SPECS, Weights
+
+# The six (a, b, c) quintic maps of ANVIL II (train/val/run.py:560-567): tuned constants that define
+# the method, kept identical.
+MAPS = (
+    (3.923798038567, -6.095026865488, 3.905234618423),
+    (3.278126713798, -3.328923386476, 0.989127286973),
+    (3.505298394150, -5.137358782410, 1.968325560615),
+    (2.815058591845, -3.685181239622, 1.417196497642),
+    (2.245503932403, -2.443826979899, 0.963091710461),
+    (2.256537145403, -2.166840097229, 0.929501253245),
+)
+RUN = (1194, 240, 50, 514)  # total, warmup, cooldown, engage steps of the schedule (run.py:568-569)
+
+
+def is_anvil_matrix(name: str, shape) -> bool:
+    return name.startswith('transformer.h.') and len(shape) == 2 and 've_gate' not in name
+
+
+def adam_scale(name: str) -> float:
+    return 300.0 if ('wte' in name or 'value_embeds' in name) else 30.0 if 'lambdas' in name else 1.0
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+class DenseGrad:
+    """A flat gradient buffer with the parameter layout, filled tensor by tensor."""
+
+    def __init__(self, w: Weights):
+        self.flat = torch.zeros_like(w.flat)
+        self.views, off = {}, 0
+        for n, s in PARAM_SPECS:
+            k = 1
+            for d in s:
+                k *= d
+            self.views[n] = self.flat[off:off + k].view(s)
+            off += k
+
+
+class AdamWDense:
+    """AdamW on dense gradients for the non-ANVIL tensors, lr = base lr x adam_scale(name)."""
+
+    def __init__(self, w: Weights, lr: float, betas, eps=1e-8, weight_decay=0.0):
+        self.w = w
+        self.m = torch.zeros_like(w.flat)
+        self.v = torch.zeros_like(w.flat)
+        self.t = 0
+        self.param_groups = []
+        groups = {}
+        for n, s in PARAM_SPECS:
+            if not is_anvil_matrix(n, s):
+                groups.setdefault(adam_scale(n), []).append(n)
+        for scale, names in groups.items():
+            self.param_groups.append(dict(names=names, lr=lr * scale, betas=tuple(betas), eps=eps,
+                                          weight_decay=weight_decay))
+
+    def step(self, grad: DenseGrad):
+        self.t += 1
+        lrs = [-1.0] * len(PARAM_SPECS)
+        index = {n: i for i, (n, _) in enumerate(PARAM_SPECS)}
+        for g in self.param_groups:
+            for n in g['names']:
+                lrs[index[n]] = float(g['lr'])
+        lr_arr = (ctypes.c_float * len(lrs))(*lrs)
+        g0 = self.param_groups[0]
+        _lib.call('noise_adamw_dense', self.w.flat.data_ptr(), self.w.packed.data_ptr(), self.m.data_ptr(),
+                  self.v.data_ptr(), grad.flat.data_ptr(), ctypes.addressof(lr_arr), float(g0['betas'][0]),
+                  float(g0['betas'][1]), float(g0['eps']), float(g0['weight_decay']), self.t, _stream(self.w.device))
+
+
+class Anvil:
+    """ANVIL II (modded-nanogpt PR #360) as in train/val/run.py:583-626."""
+
+    def __init__(self, w: Weights, lr: float, weight_decay: float, steps: int, lane_beta=0.9, beta_min=0.85,
+                 beta_max=0.93, slow_beta=0.98, fast_beta=0.85, fast_weight=0.4385):
+        self.w = w
+        self.param_groups = [dict(lr=lr, weight_decay=weight_decay)]
+        self.total, self.warmup, self.cooldown, self.engage = (round(k * steps / RUN[0]) for k in RUN)
+        self.lane_beta, self.beta_min, self.beta_max = lane_beta, beta_min, beta_max
+        self.slow_beta, self.fast_beta, self.fast_weight = slow_beta, fast_beta, fast_weight
+        self.t = 0
+        dev = w.device
+        tiles, lanes, mats = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+        _lib.call('noise_anvil_sizes', ctypes.addressof(tiles), ctypes.addressof(lanes), ctypes.addressof(mats))
+        self.fast = torch.zeros_like(w.flat)
+        self.slow = torch.zeros_like(w.flat)
+        self.scratch = torch.zeros_like(w.flat)
+        self.x = torch.zeros(w.flat.numel(), dtype=torch.bfloat16, device=dev)
+        self.energy = torch.zeros(lanes.value, dtype=torch.float32, device=dev)
+        self.partials = torch.zeros(2 * tiles.value, dtype=torch.float32, device=dev)
+        self.scalars = torch.zeros(mats.value, dtype=torch.float32, device=dev)
+        # views of x per matrix, grouped by shape for batched maps
+        self.wide, self.tall, off = {}, {}, 0
+        for n, s in PARAM_SPECS:
+            k = s[0] * (s[1] if len(s) > 1 else 1)
+            if is_anvil_matrix(n, s):
+                (self.tall if s[0] > s[1] else self.wide).setdefault(s, []).append(self.x[off:off + k].view(s))
+            off += k
+
+    def rail_beta(self):
+        lo, hi, cool = self.beta_min, self.beta_max, self.total - self.cooldown
+        if self.t < self.warmup:
+            return lo + (hi - lo) * self.t / self.warmup
+        if self.t > cool:
+            return hi - (hi - lo) * (self.t - cool) / self.cooldown
+        return hi
+
+    def _polar_maps(self):
+        for group, tall in ((self.wide, False), (self.tall, True)):
+            for views in group.values():
+                x = torch.stack(views)
+                for a, b, c in MAPS:
+                    if tall:
+                        s = x.transpose(-1, -2) @ x
+                        x = a * x + x @ (b * s + c * s @ s)
+                    else:
+                        s = x @ x.transpose(-1, -2)
+                        x = a * x + (b * s + c * s @ s) @ x
+                for v, xi in zip(views, x):
+                    v.copy_(xi)
+
+    @torch.no_grad()
+    def step(self, grad: DenseGrad):
+        beta, engaged = self.rail_beta(), self.t >= self.engage
+        fast_beta, weight = (self.fast_beta, self.fast_weight) if engaged else (beta, 1.0)
+        dev = self.w.device
+        g = self.param_groups[0]
+        _lib.call('noise_anvil_prepare', grad.flat.data_ptr(), self.fast.data_ptr(), self.slow.data_ptr(),
+                  self.scratch.data_ptr(), self.x.data_ptr(), self.partials.data_ptr(), self.scalars.data_ptr(),
+                  float(fast_beta), float(self.slow_beta), float(beta), float(weight), _stream(dev))
+        self._polar_maps()
+        _lib.call('noise_anvil_finish', self.w.flat.data_ptr(), self.w.packed.data_ptr(), self.slow.data_ptr(),
+                  self.x.data_ptr(), self.energy.data_ptr(), self.partials.data_ptr(), self.scalars.data_ptr(),
+                  float(self.lane_beta), float(g['lr']), float(g['weight_decay']), _stream(dev))
+        self.t += 1
+
+
+class Optimizers:
+    """run.py:629-640: both optimizers behind one step(); param_groups concatenated for set_rate."""
+
+    def __init__(self, *optimizers):
+        self.optimizers = optimizers
+        self.param_groups = [g for o in optimizers for g in o.param_groups]
+
+    def zero_grad(self, set_to_none=True):
+        pass
+
+    def step(self, grad: DenseGrad):
+        for o in self.optimizers:
+            o.step(grad)
+
+
+def make_optimizer(w: Weights, lr: float, betas, anvil_lr: float, anvil_wd: float, steps: int) -> Optimizers:
+    """ANVIL II on block matrices, AdamW elsewhere (run.py:643-656)."""
+    return Optimizers(Anvil(w, anvil_lr, anvil_wd, steps), AdamWDense(w, lr, betas, eps=1e-8, weight_decay=0.0))

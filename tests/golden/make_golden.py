@@ -11,6 +11,10 @@ on CPU in float32 and saves their outputs as small .npz fixtures beside this scr
                    CHUNK = 1, two sequences of T = 384, step 1 -> member losses, the gradients handed
                    to AdamW (full for small tensors, checksums and sampled entries for matrices) and
                    the parameter change after AdamW.
+  optim.npz        train/val/run.py make_optimizer (ANVIL II on block matrices, AdamW x1/x30/x300
+                   elsewhere), three steps on seeded dense gradients (torch.Generator seed 11, N(0, 0.01^2),
+                   drawn in named_parameters order each step): parameter deltas per tensor as checksums
+                   and 512 sampled entries.
   dust.npz         train/val/run.py DUST pieces on two sequences of T = 128: orthogonal_noise with
                    injected frames and signs, coordinate_differences, reward_to_go, and
                    direct_errors (real capture + rerun + centring + contraction) for a writers group,
@@ -66,10 +70,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', type=Path, required=True)
     ap.add_argument('--only-dust', action='store_true')
+    ap.add_argument('--only-optim', action='store_true')
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
     if args.only_dust:
         dust_golden(args.reference)
+        raise SystemExit
+    if args.only_optim:
+        optim_golden()
         raise SystemExit
     import utils.model as um
     import train.val.eggroll as eg
@@ -228,6 +236,28 @@ def dust_golden(reference):
     print('dust', {k: v.shape for k, v in out.items() if k.startswith('de_')})
 
 
+def optim_golden():
+    torch._dynamo.config.disable = True
+    import train.val.run as run
+    model = run.make_model(torch.device('cpu'), SEED)
+    opt = run.make_optimizer(model, run.recipe(0.01), 100)
+    before = {n: p.detach().clone() for n, p in model.named_parameters()}
+    g = torch.Generator().manual_seed(11)
+    for _ in range(3):
+        for _, prm in model.named_parameters():
+            prm.grad = torch.randn(prm.shape, generator=g) * 0.01
+        opt.step()
+    out = {}
+    for i, (n, prm) in enumerate(model.named_parameters()):
+        d = (prm.detach() - before[n]).double()
+        out[f'd{i}_sums'] = checksums(d)
+        idx, vals = sample_entries(d, n=512, seed=100 + i)
+        out[f'd{i}_idx'], out[f'd{i}_val'] = idx.astype(np.int32), vals.astype(np.float32)
+    np.savez_compressed(HERE / 'optim.npz', **out)
+    print('optim', out['d3_sums'], out['d2_sums'])
+
+
 if __name__ == '__main__':
     main()
     dust_golden(None)
+    optim_golden()
