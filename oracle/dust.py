@@ -2,7 +2,7 @@
 
 Reference: `train/val/run.py` — hadamard :143-152, orthogonal_noise :223-238, reward_to_go :81-86,
 head_loss :89-94, block_forward :102-117, coordinate_differences :120-137, rerun :256-279,
-direct_errors :332-378 (without the credit-memory prior), reassemble :465-471.
+direct_errors :332-378 (without the credit-memory prior), local_errors :391-463, reassemble :465-471.
 
 Frames and signs of the orthogonal draws come from the counter-based stream (noise_b200's
 `csrc/dust.cuh` generates the same bits); parity with the reference is shown by injecting them into
@@ -234,3 +234,101 @@ def reassemble_embedding(error: torch.Tensor, idx: torch.Tensor, vocab: int = om
     """Embedding gradient: rows of the error summed per token id (run.py:468-470, index_add)."""
     out = torch.zeros(vocab, error.shape[-1], dtype=torch.float64)
     return out.index_add_(0, idx.reshape(-1), error.reshape(-1, error.shape[-1]).double())
+
+
+LOCAL_SITES = {'q': 'attn.c_q', 'k': 'attn.c_k', 'v': 'attn.c_v', 'gate': 'attn.ve_gate'}
+
+
+def local_layers(kind: str):
+    """Blocks with an estimate of `kind` (run.py:398): value embeddings and gates exist on VE blocks only."""
+    return [i for i in range(om.LAYERS) if kind not in ('ve', 'gate') or i in om.VE_LAYERS]
+
+
+def local_site(kind: str, i: int) -> str:
+    return f'value_embeds.{i}' if kind == 've' else f'transformer.h.{i}.{LOCAL_SITES[kind]}'
+
+
+def local_width(kind: str) -> int:
+    return om.HEADS if kind == 'gate' else om.WIDTH
+
+
+def attention_inputs(p: dict, cap: dict, idx, i: int):
+    """Block i's raw q, k, v [b, t, h, d], gate logits z [b, t, h] and value-embedding rows (None off
+    the VE blocks), recomputed from the captured block input (run.py:418-425)."""
+    b, t = idx.shape
+    pre = f'transformer.h.{i}.'
+    h = om.rms_norm(cap['blocks'][i])
+    q, k, v = ((h @ p[pre + f'attn.c_{n}.weight'].t()).view(b, t, om.HEADS, om.HEAD_DIM) for n in 'qkv')
+    z = ve = None
+    if i in om.VE_LAYERS:
+        z = h[..., :om.GATE_CHANNELS] @ p[pre + 'attn.ve_gate.weight'].t()
+        ve = p[f'value_embeds.{i}.weight'][idx].view(b, t, om.HEADS, om.HEAD_DIM)
+    return q, k, v, z, ve
+
+
+def local_credit(t: int, window: int, gamma: float) -> torch.Tensor:
+    """credit[t', s] = gamma^(s - t') for 0 <= s - t' <= window (run.py:428-430)."""
+    pos = torch.arange(t)
+    lag = pos[None, :] - pos[:, None]
+    return ((lag >= 0) & (lag <= window)).double() * gamma ** lag.clamp(min=0).double()
+
+
+def local_errors(p: dict, cap: dict, idx, kind: str, draws_by_layer: dict, targets: dict, sigma: float = 0.1,
+                 gamma: float = 0.98, n: int = 16) -> dict:
+    """Attention-internal errors of one kind (run.py:391-463) for every block that has it, from the
+    draws a [N, b, t, width] given per block, scored against the hub targets [b, t, 512]:
+      q, k   delta = attention with the perturbed (RoPE'd, normed) side minus the clean attention
+      v, ve  delta = attention of the value change sigma a (ve: x 2 sigmoid(z))
+      gate   delta = attention of (2 sigmoid(z + sigma a) - 2 sigmoid(z - sigma a)) ve, divisor 2 sigma
+    score = <target, delta> per head; all kinds but q spread it back over earlier tokens by the lag
+    credit; errors = sum_draws score a / divisor / N. Returns {site: [b, t, width]} in float64."""
+    b, t = idx.shape
+    cos, sin = om.rotary_tables(t)
+    h, d = om.HEADS, om.HEAD_DIM
+    processed = lambda raw: om.rms_norm(om.rope(raw, cos, sin))  # noqa: E731
+    out = {}
+    for i in local_layers(kind):
+        q, k, v, z, ve = attention_inputs(p, cap, idx, i)
+        values = v if z is None else v + (2 * torch.sigmoid(z)).unsqueeze(-1) * ve
+        qp, kp = processed(q), processed(k)
+        window = om.WINDOWS[i]
+        baseline = om.window_attention(qp, kp, values, window)
+        credit = local_credit(t, window, gamma)
+        tgt = targets[i].view(b, t, h, d).double()
+        a_all = draws_by_layer[i].float()
+        total = a_all.shape[0]
+        err = torch.zeros(b, t, local_width(kind), dtype=torch.float64)
+        rep = lambda x, m: x.unsqueeze(0).expand(m, *x.shape).reshape(m * b, t, h, d)  # noqa: E731
+        for c0 in range(0, total, n):
+            a = a_all[c0:c0 + n]
+            m = a.shape[0]
+            divisor = sigma
+            if kind in ('q', 'k'):
+                raw = q if kind == 'q' else k
+                moved = processed((raw.unsqueeze(0) + sigma * a.view(m, b, t, h, d)).reshape(m * b, t, h, d))
+                qa, ka = (moved, rep(kp, m)) if kind == 'q' else (rep(qp, m), moved)
+                delta = om.window_attention(qa, ka, rep(values, m), window).view(m, b, t, h, d) - baseline
+            else:
+                if kind == 'gate':
+                    dv = (2 * torch.sigmoid(z + sigma * a) - 2 * torch.sigmoid(z - sigma * a)).unsqueeze(-1) * ve
+                    divisor = 2 * sigma
+                else:
+                    dv = sigma * a.view(m, b, t, h, d)
+                    if kind == 've':
+                        dv = dv * (2 * torch.sigmoid(z)).unsqueeze(-1)
+                delta = om.window_attention(rep(qp, m), rep(kp, m), dv.reshape(m * b, t, h, d),
+                                            window).view(m, b, t, h, d)
+            score = torch.einsum('bthd,nbthd->nbth', tgt, delta.double())
+            if kind != 'q':
+                score = torch.einsum('nbsh,ts->nbth', score, credit)
+            est = torch.einsum('nbth,nbthd->bthd', score, a.double().view(m, b, t, h, -1))
+            err += est.reshape(b, t, -1) / divisor
+        out[local_site(kind, i)] = err / total
+    return out
+
+
+def local_input(cap: dict, kind: str, i: int) -> torch.Tensor:
+    """The cached input of a local site's module: the block's normed input (its first 32 channels for
+    the gate); value embeddings reassemble by token id instead."""
+    h = om.rms_norm(cap['blocks'][i])
+    return h[..., :om.GATE_CHANNELS] if kind == 'gate' else h

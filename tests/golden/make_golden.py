@@ -20,6 +20,9 @@ on CPU in float32 and saves their outputs as small .npz fixtures beside this scr
                    direct_errors (real capture + rerun + centring + contraction) for a writers group,
                    an MLP hidden site (live-unit mask), the embedding (rerun from the embedding) and
                    an attention-output hub with reward-to-go, each with its reassembled gradient.
+  local.npz        train/val/run.py DUST.local_errors for each kind (q, k, v, gate, ve) with injected
+                   draws and seeded hub targets (LOCAL_CASES), plus the first block's reassembled
+                   gradient per kind.
 
 Only the attention primitive is swapped, for the mathematically identical masked SDPA
 (`(q >= k) & (q - k <= window)`), because torch.compile(flex_attention) does not lower on CPU here;
@@ -71,6 +74,7 @@ def main():
     ap.add_argument('--reference', type=Path, required=True)
     ap.add_argument('--only-dust', action='store_true')
     ap.add_argument('--only-optim', action='store_true')
+    ap.add_argument('--only-local', action='store_true')
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
     if args.only_dust:
@@ -78,6 +82,9 @@ def main():
         raise SystemExit
     if args.only_optim:
         optim_golden()
+        raise SystemExit
+    if args.only_local:
+        local_golden(args.reference)
         raise SystemExit
     import utils.model as um
     import train.val.eggroll as eg
@@ -159,6 +166,83 @@ def main():
     print('eggroll step', mean_loss, torch.cat(seen_losses).tolist())
 
 
+def pack(out: dict, limit: int = 8192, samples: int = 4096) -> dict:
+    """Large arrays become checksums + sampled entries (key__sums, __idx, __val, __shape)."""
+    packed = {}
+    for k, v in out.items():
+        v = np.asarray(v)
+        if v.size > limit:
+            t_ = torch.from_numpy(v.astype(np.float64))
+            idx, vals = sample_entries(t_, n=samples, seed=len(k))
+            packed[k + '__sums'] = checksums(t_)
+            packed[k + '__idx'], packed[k + '__val'] = idx, vals
+            packed[k + '__shape'] = np.array(v.shape)
+        else:
+            packed[k] = v
+    return packed
+
+
+def injector(run, est):
+    """A stand-in for DUST.orthogonal_noise that runs the reference's own function on frames and
+    signs taken from the counter-based stream (world 1)."""
+    from oracle import dust as od
+
+    def inject(site, draws, chunk, n, b_, t_, d, dtype=None):
+        sid = od.site_id(site)
+        cycles = -(-draws // d)
+        pats, offs = od.frame(SEED, STEP, sid, cycles, d, b_, t_)
+        idx = chunk * n + np.arange(n)
+        signs = od.draw_signs(SEED, STEP, sid, idx, b_, t_)
+        est.frames[site] = (pats, offs)
+        orig = est.signs
+        est.signs = lambda *shape, shared=False: signs[..., None] if shape == (n, b_, t_, 1) else orig(*shape, shared=shared)
+        try:
+            a = run.DUST.orthogonal_noise(est, site, draws, chunk, n, b_, t_, d, dtype)
+        finally:
+            est.signs = orig
+        return a
+
+    return inject
+
+
+# (kind, sequences, length, draws): windows bind at T = 1152; T = 256, 512 and 1152 cover the GPU
+# kernel's 2-, 4- and 1-tile CTAs
+LOCAL_CASES = [('q', 2, 256, 32), ('k', 1, 1152, 16), ('v', 2, 256, 16), ('gate', 2, 256, 16), ('ve', 1, 512, 16)]
+LOCAL_TARGET_SEED = 21
+
+
+def local_targets(b: int, t: int, layers: int = 8) -> dict:
+    """Seeded stand-ins for the hub targets, [b, t, 512] per block, 0.01 N(0, 1)."""
+    g = torch.Generator().manual_seed(LOCAL_TARGET_SEED)
+    return {i: torch.randn(b, t, 512, generator=g) * 0.01 for i in range(layers)}
+
+
+def local_golden(reference):
+    """DUST.local_errors (train/val/run.py:391-463) per kind with injected draws and seeded targets,
+    and each kind's reassembled gradient of its first block."""
+    torch._dynamo.config.disable = True
+    import train.val.run as run
+    run.attention = sdpa_window
+    torch.set_num_threads(8)
+    out = {}
+    for kind, b, t, draws in LOCAL_CASES:
+        model = run.make_model(torch.device('cpu'), SEED)
+        est = run.DUST(model, run.recipe(0.01), SEED, 0, 1)
+        rows = zipf_tokens(b, t + 1, seed=5)
+        x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+        est.capture(x, y)
+        est.orthogonal_noise = injector(run, est)
+        with torch.no_grad():
+            errs = est.local_errors(kind, draws, local_targets(b, t))
+        for k, (site, e) in enumerate(errs.items()):
+            out[f'le_{kind}_{k}'] = e.numpy()
+        site, e = next(iter(errs.items()))
+        out[f'lr_{kind}'] = est.reassemble(site, e).numpy()
+        out[f'le_{kind}_meta'] = np.array([b, t, draws])
+        print('local', kind, {s: float(v.abs().mean()) for s, v in errs.items()})
+    np.savez_compressed(HERE / 'local.npz', **pack(out, samples=1024))
+
+
 def dust_golden(reference):
     """DUST fixtures; only orthogonal_noise's random frames and signs are injected."""
     from oracle import dust as od
@@ -176,21 +260,7 @@ def dust_golden(reference):
     out = dict(tokens=rows.numpy().astype(np.int16), targets=y.numpy().astype(np.int64),
                clean_loss=est.clean_loss.numpy())
 
-    def inject(site, draws, chunk, n, b_, t_, d, dtype=None):
-        sid = od.site_id(site)
-        total = draws  # world 1
-        cycles = -(-total // d)
-        pats, offs = od.frame(SEED, STEP, sid, cycles, d, b_, t_)
-        idx = chunk * n + np.arange(n)
-        signs = od.draw_signs(SEED, STEP, sid, idx, b_, t_)
-        est.frames[site] = (pats, offs)
-        orig = est.signs
-        est.signs = lambda *shape, shared=False: signs[..., None] if shape == (n, b_, t_, 1) else orig(*shape, shared=shared)
-        try:
-            a = run.DUST.orthogonal_noise(est, site, draws, chunk, n, b_, t_, d, dtype)
-        finally:
-            est.signs = orig
-        return a
+    inject = injector(run, est)
 
     # orthogonal_noise itself
     a = inject('transformer.h.1.mlp.c_fc', 96, 1, 16, b, t, 2048)
@@ -221,18 +291,7 @@ def dust_golden(reference):
             if not site.startswith('o@'):
                 out[f'ra_{name}_{k}'] = est.reassemble(site, errs[site]).numpy()
         out[f'de_{name}_meta'] = np.array([draws, sigma, -1 if entry is None else entry, gamma])
-    packed = {}
-    for k, v in out.items():
-        v = np.asarray(v)
-        if v.size > 8192:  # large arrays: checksums + 4096 sampled entries keep the fixture small
-            t_ = torch.from_numpy(v.astype(np.float64))
-            idx, vals = sample_entries(t_, n=4096, seed=len(k))
-            packed[k + '__sums'] = checksums(t_)
-            packed[k + '__idx'], packed[k + '__val'] = idx, vals
-            packed[k + '__shape'] = np.array(v.shape)
-        else:
-            packed[k] = v
-    np.savez_compressed(HERE / 'dust.npz', **packed)
+    np.savez_compressed(HERE / 'dust.npz', **pack(out))
     print('dust', {k: v.shape for k, v in out.items() if k.startswith('de_')})
 
 
