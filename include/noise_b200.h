@@ -117,6 +117,41 @@ int noise_dust_errors(const float* clean, const float* perturbed, int draws, int
 int noise_coordinate_differences(const float* raw, const int32_t* targets, int64_t rows, float sigma, float* out,
                                  void* stream);
 
+/* DUST's attention-internal errors (replaces DUST.local_errors, train/val/run.py:391-463). One block,
+ * one kind: 0 q, 1 k, 2 v, 3 gate, 4 value embedding (3 and 4 on blocks 1, 3, 5, 7 only). All
+ * [B*T, 512] operands are bf16 rows of B sequences of T tokens (T % 128 == 0), 16-byte aligned. */
+typedef struct NoiseLocal {
+  int kind;
+  int layer;                /* block: sets the attention window */
+  uint32_t site;            /* stream site id of the draws (the tensor id of the site's weight) */
+  float sigma;              /* draw scale (0.1) */
+  float gamma;              /* lag credit decay per token (0.98) */
+  const void* raw;          /* kinds q, k: raw c_q / c_k outputs before RoPE and norm */
+  const void* q;            /* processed clean queries: rms_norm(rope(raw q)) per head */
+  const void* k;            /* processed clean keys */
+  const void* values;       /* clean values v + 2 sigmoid(z) ve */
+  const float* gate_logits; /* kinds gate, ve: [B*T][8] fp32 */
+  const float* ve;          /* kinds gate, ve: [B*T][512] fp32 value-embedding rows */
+  const void* target;       /* the block's hub target */
+  const float* base;        /* kinds q, k: [B*T][8] clean scores from noise_local_baseline */
+} NoiseLocal;
+
+/* out = bf16(rms_norm(rope(raw))) per head: the reference's `processed` (run.py:405-406). */
+int noise_local_process(const void* raw, const float* rope, int B, int T, void* out, void* stream);
+
+/* base[b*T + t][h] = <target, attention(q, k, values)> at (b, t, head h): the clean scores. */
+int noise_local_baseline(const NoiseLocal* spec, int B, int T, float* base, int* status, void* stream);
+
+/* Workspace of noise_local_errors for `draws` draws. */
+int64_t noise_local_workspace_bytes(int B, int T, int draws);
+
+/* errors [B*T][width] += sum over draws [draw_begin, draw_begin + draws) (draws <= 1024) of the
+ * credited score times the draw / divisor (sigma; 2 sigma for the gate); width 8 for the gate, else
+ * 512. The caller divides by the total draw count. */
+int noise_local_errors(const NoiseLocal* spec, const float* rope, int B, int T, int64_t draw_begin, int draws,
+                       uint32_t seed, uint32_t step, float* errors, void* workspace, size_t ws_bytes, int* status,
+                       void* stream);
+
 /* Replaces torch.optim.AdamW.step on dense gradients (the DUST estimator's; train/val/run.py:652-655):
  * grad is a full flat gradient buffer; lr_per_tensor[60] gives each tensor's learning rate, < 0
  * for tensors another optimizer owns. adam_t is the 1-based step for the bias corrections. */

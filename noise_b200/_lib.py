@@ -40,6 +40,11 @@ SIGNATURES: dict[str, tuple] = {
     'noise_dust_errors': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_uint32, c_int, c_float,
                                   c_float, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
     'noise_coordinate_differences': (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p, c_void_p]),
+    'noise_local_process': (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    'noise_local_baseline': (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    'noise_local_workspace_bytes': (c_int64, [c_int, c_int, c_int]),
+    'noise_local_errors': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int64, c_int, c_uint32, c_uint32, c_void_p,
+                                   c_void_p, c_size_t, c_void_p, c_void_p]),
     'noise_adamw_dense': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_float,
                                   c_float, c_float, c_int, c_void_p]),
     'noise_anvil_sizes': (c_int, [c_void_p, c_void_p, c_void_p]),
@@ -68,6 +73,13 @@ class NoiseDirect(ctypes.Structure):
     """struct NoiseDirect of include/noise_b200.h."""
     _fields_ = [('entry', ctypes.c_int), ('mask', ctypes.c_uint32), ('site', ctypes.c_uint32 * 5),
                 ('sigma', ctypes.c_float), ('x_entry', c_void_p), ('inv0', c_void_p), ('live', c_void_p)]
+
+
+class NoiseLocal(ctypes.Structure):
+    """struct NoiseLocal of include/noise_b200.h."""
+    _fields_ = [('kind', ctypes.c_int), ('layer', ctypes.c_int), ('site', ctypes.c_uint32), ('sigma', ctypes.c_float),
+                ('gamma', ctypes.c_float)] + [(n, c_void_p) for n in ('raw', 'q', 'k', 'values', 'gate_logits', 've',
+                                                                       'target', 'base')]
 
 
 class NoiseCapture(ctypes.Structure):

@@ -16,6 +16,11 @@
 // offset 8: no running maximum and no rescaling of the TMEM accumulator. 32-key chunks outside a
 // warp's rows' windows skip their exponentials. TMEM: group g uses S at 128g and O at 128g + 64.
 // Every wait is bounded (status word on timeout).
+//
+// Score mode (kScore, DUST's attention reruns, train/val/run.py:391-463): Q, K and V each come from
+// their own [rows, 512] map, and CTA row block z reads operand X's sequence z % mod_X (mod 0: z), so
+// per-draw operands and shared clean ones mix in one launch. Instead of y, each query row writes
+// score[z * T + q][head] = <target, O> - base (target and base of the clean sequence z % seqs).
 #pragma once
 
 #include "model_layout.cuh"
@@ -29,6 +34,13 @@ struct AttnTcParams {
   float* ystats;     // [rows][8]
   int layer, window;
   int* status;
+  int col_q, col_k, col_v;  // column of head 0 in each operand's map
+  int mod_q, mod_k, mod_v;  // row block of operand X = blockIdx.z % mod_X (0: blockIdx.z)
+  // score mode
+  const __nv_bfloat16* target;  // [seqs * T, 512]
+  const float* base;            // [seqs * T][8] or nullptr
+  float* score;                 // [gridDim.z * T][8]
+  int seqs;
 };
 
 constexpr int kAtQ = 128, kAtK = 64, kAtStages = 3;
@@ -44,9 +56,10 @@ struct AttnTcLayout {
   static constexpr uint32_t kTmemCols = 128 * G;
 };
 
-template <int G>
+template <int G, bool kScore>
 __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G == 4 ? 112 : 168)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ AttnTcParams p) {
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnTcParams p) {
   using L = AttnTcLayout<G>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -74,6 +87,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
   const int unit = n_units - 1 - blockIdx.x;  // longest key ranges first
   const int head = blockIdx.y;
   const int64_t row_base = (int64_t)blockIdx.z * T;
+  auto operand_rows = [&](int mod) { return (int64_t)(mod ? (int)blockIdx.z % mod : (int)blockIdx.z) * T; };
   const int q0 = unit * kAtQ * G;  // first query of the CTA
   const int kt_begin = max(0, q0 - p.window) / kAtK;
   const int kt_end = (q0 + kAtQ * G - 1) / kAtK;
@@ -93,9 +107,11 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
-    prefetch_tensormap(&tm_qkv);
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
   }
-  if (tid >= 64 && tid < 80) {  // the member's c_proj column factor for this head's 64 columns
+  if (!kScore && tid >= 64 && tid < 80) {  // the member's c_proj column factor for this head's 64 columns
     const RowInfo r0 = row_info(p.ctx, row_base);
     reinterpret_cast<float4*>(bproj)[tid - 64] =
         gauss4(p.ctx.key, (head * kHeadDim >> 2) + (tid - 64), tid_proj(p.layer), 1, r0.direction);
@@ -109,22 +125,23 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int qcol = head * kHeadDim, kcol = kWidth + head * kHeadDim, vcol = 2 * kWidth + head * kHeadDim;
+  const int qcol = p.col_q + head * kHeadDim, kcol = p.col_k + head * kHeadDim, vcol = p.col_v + head * kHeadDim;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
+      const int64_t rq = operand_rows(p.mod_q), rk = operand_rows(p.mod_k), rv = operand_rows(p.mod_v);
       mbar_arrive_expect_tx(q_full, G * kAtQBytes);
       for (int b = 0; b < 2 * G; ++b)
-        tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_qkv, q_full, qcol, (int)(row_base + q0 + 64 * b));
+        tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_q, q_full, qcol, (int)(rq + q0 + 64 * b));
       int issued = 0;
       for (int j = 0; j < n_kt; ++j) {
         const int st = j % kAtStages;
         if (!mbar_wait(&kv_empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, status)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kAtTileBytes);
-        const int r = (int)(row_base + (kt_begin + j) * kAtK);
-        tma_load_2d(sK + st * kAtTileBytes, &tm_qkv, &kv_full[st], kcol, r);
-        tma_load_2d(sV + st * kAtTileBytes, &tm_qkv, &kv_full[st], vcol, r);
+        const int r = (kt_begin + j) * kAtK;
+        tma_load_2d(sK + st * kAtTileBytes, &tm_k, &kv_full[st], kcol, (int)(rk + r));
+        tma_load_2d(sV + st * kAtTileBytes, &tm_v, &kv_full[st], vcol, (int)(rv + r));
         issued = j + 1;
       }
       // copies in flight land before the CTA can exit
@@ -248,7 +265,30 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g]);
     }
-    if (ok && mbar_wait(o_full, 0, abort_flag, status)) {
+    if (kScore) {
+      if (ok && mbar_wait(o_full, 0, abort_flag, status)) {
+        tc_fence_after();
+        float o[64];
+        tmem_ld64(tO + lane_addr, o);
+        const float inv = 1.0f / ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
+        const int64_t trow = (int64_t)((int)blockIdx.z % p.seqs) * T + q;
+        const uint4* tg = reinterpret_cast<const uint4*>(p.target + trow * kWidth + head * kHeadDim);
+        float d = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 u = __ldg(tg + c);
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i]));
+            d += o[8 * c + 2 * i] * f.x + o[8 * c + 2 * i + 1] * f.y;
+          }
+        }
+        d *= inv;
+        if (p.base) d -= __ldg(p.base + trow * kHeads + head);
+        p.score[(row_base + q) * kHeads + head] = d;
+      }
+    } else if (ok && mbar_wait(o_full, 0, abort_flag, status)) {
       tc_fence_after();
       float o[64];
       tmem_ld64(tO + lane_addr, o);

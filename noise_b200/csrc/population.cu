@@ -258,14 +258,14 @@ int launch_attention_g(const CUtensorMap& tm, const AttnTcParams& ap, int64_t ro
   using L = AttnTcLayout<G>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attention_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
+    if (cudaFuncSetAttribute(attention_tc_kernel<G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
         cudaSuccess)
       return kStatusLaunchFailed;
     configured = true;
   }
   dim3 grid(ap.ctx.T / (kAtQ * G), kHeads, (unsigned)(rows / ap.ctx.T));
   LaunchScope scope(kKindAttention, stream);
-  attention_tc_kernel<G><<<grid, L::kThreads, L::kSmem, stream>>>(tm, ap);
+  attention_tc_kernel<G, false><<<grid, L::kThreads, L::kSmem, stream>>>(tm, tm, tm, ap);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
 
@@ -274,7 +274,10 @@ int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& 
   CUtensorMap tm;
   if (make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, 64, kHeadDim))
     return kStatusBadArgument;
-  AttnTcParams ap{ctx, w.y, w.ystats, layer, layer_window(layer), status};
+  AttnTcParams ap{};
+  ap.ctx = ctx, ap.y = w.y, ap.ystats = w.ystats, ap.layer = layer, ap.window = layer_window(layer);
+  ap.status = status;
+  ap.col_q = 0, ap.col_k = kWidth, ap.col_v = 2 * kWidth;
   const int n_qt = ctx.T / kAtQ;  // query tiles per sequence; a CTA takes 4, 2 or 1 of them
   if (n_qt % 4 == 0) return launch_attention_g<4>(tm, ap, rows, stream);
   if (n_qt % 2 == 0) return launch_attention_g<2>(tm, ap, rows, stream);

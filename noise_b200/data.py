@@ -17,3 +17,22 @@ def zipf_tokens(rows: int, length: int = 2049, s: float = 1.1, vocab: int = 4096
     perm = torch.randperm(vocab, generator=g)
     samples = torch.multinomial(probs, rows * length, replacement=True, generator=g)
     return perm[samples].view(rows, length)
+
+
+TRAIN_ROWS, VAL_ROWS, ROW = 4880, 544, 2049  # utils/prepare_data.py:19-21 (rows of 2049 tokens)
+
+
+def load_rows(path, rows: int, synthetic: bool, seed: int) -> torch.Tensor:
+    """The FineWeb token rows of utils/prepare_data.py:load_rows (shape-checked), or seeded Zipf(1.1)
+    rows of the same shape when the file is absent and `synthetic` is set."""
+    from pathlib import Path
+    path = Path(path)
+    if path.exists():
+        data = torch.load(path)
+        if tuple(data.shape) != (rows, ROW):
+            raise ValueError(f'{path}: expected [{rows}, {ROW}], got {list(data.shape)}')
+        return data
+    if not synthetic:
+        raise FileNotFoundError(f'{path} is missing (prepare the data, or pass --synthetic)')
+    return zipf_tokens(rows, ROW, seed=seed)
+

@@ -178,6 +178,122 @@ def reassemble(cap: Capture, name: str, error: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------------------------------------
+# attention-internal (local) errors
+# ------------------------------------------------------------------------------------------------
+LOCAL_KINDS = {'q': 0, 'k': 1, 'v': 2, 'gate': 3, 've': 4}
+LOCAL_SITES = {'q': 'attn.c_q', 'k': 'attn.c_k', 'v': 'attn.c_v', 'gate': 'attn.ve_gate'}
+PACK_LAYER = 3 * WIDTH * WIDTH + WIDTH * WIDTH + 2 * HIDDEN * WIDTH  # packed bf16 weights per block
+VE_LAYERS = (1, 3, 5, 7)
+
+
+def local_layers(kind: str) -> list[int]:
+    """Blocks with an estimate of `kind` (run.py:398): gates and value embeddings on VE blocks only."""
+    return [i for i in range(LAYERS) if kind not in ('ve', 'gate') or i in VE_LAYERS]
+
+
+def local_site(kind: str, layer: int) -> str:
+    return f'value_embeds.{layer}' if kind == 've' else f'transformer.h.{layer}.{LOCAL_SITES[kind]}'
+
+
+class LocalInputs:
+    """Block `layer`'s clean attention inputs from the captured block input (run.py:418-425): the raw
+    c_q / c_k / c_v outputs (bf16, one GEMM on the packed weights), the gate logits and value-embedding
+    rows on VE blocks, the processed queries and keys and the clean values."""
+
+    def __init__(self, w: Weights, cap: Capture, layer: int):
+        dev, rows = w.device, cap.B * cap.T
+        self.layer = layer
+        x = cap.blocks[layer]
+        self.h = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + torch.finfo(torch.float32).eps)
+        hb = self.h.bfloat16().contiguous()
+        qkv = torch.empty(rows, 3 * WIDTH, dtype=torch.bfloat16, device=dev)
+        wq = w.packed[layer * PACK_LAYER: layer * PACK_LAYER + 3 * WIDTH * WIDTH]
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.call('noise_gemm_bf16', hb.data_ptr(), wq.data_ptr(), qkv.data_ptr(), rows, 3 * WIDTH, WIDTH, 1.0, 1,
+                  status.data_ptr(), _stream(dev))
+        self.raw = {n: qkv[:, i * WIDTH:(i + 1) * WIDTH].contiguous() for i, n in enumerate('qkv')}
+        self.z = self.ve = None
+        values = self.raw['v']
+        if layer in VE_LAYERS:
+            gw = w.views[f'transformer.h.{layer}.attn.ve_gate.weight']
+            self.z = (hb[:, :32] @ gw.bfloat16().t()).float().contiguous()
+            self.ve = w.views[f'value_embeds.{layer}.weight'][cap.x.reshape(-1).long()].contiguous()
+            values = (values.float() + (2 * torch.sigmoid(self.z)).repeat_interleave(64, 1) * self.ve).bfloat16()
+        self.values = values.contiguous()
+        rope = w.rope(cap.T)
+        self.processed = {}
+        for n in 'qk':
+            out = torch.empty(rows, WIDTH, dtype=torch.bfloat16, device=dev)
+            _lib.call('noise_local_process', self.raw[n].data_ptr(), rope.data_ptr(), cap.B, cap.T, out.data_ptr(),
+                      _stream(dev))
+            self.processed[n] = out
+        self.bases = {}
+
+    def spec(self, kind: str, target: torch.Tensor, sigma: float, gamma: float) -> _lib.NoiseLocal:
+        s = _lib.NoiseLocal()
+        s.kind, s.layer = LOCAL_KINDS[kind], self.layer
+        s.site = TENSOR_ID[local_site(kind, self.layer) + '.weight']
+        s.sigma, s.gamma = sigma, gamma
+        s.raw = self.raw[kind].data_ptr() if kind in ('q', 'k') else None
+        s.q, s.k, s.values = self.processed['q'].data_ptr(), self.processed['k'].data_ptr(), self.values.data_ptr()
+        if self.z is not None:
+            s.gate_logits, s.ve = self.z.data_ptr(), self.ve.data_ptr()
+        s.target = target.data_ptr()
+        return s
+
+    def input_of(self, kind: str) -> torch.Tensor:
+        """The site module's cached input: the normed block input (first 32 channels for the gate)."""
+        return self.h[:, :32] if kind == 'gate' else self.h
+
+
+def local_errors(w: Weights, cap: Capture, kind: str, draws: int, targets: dict, seed: int, step: int,
+                 draw_offset: int = 0, sigma: float = 0.1, gamma: float = 0.98, inputs: dict | None = None,
+                 max_workspace: int = 4 << 30) -> dict[str, torch.Tensor]:
+    """DUST.local_errors (run.py:391-463): {site: [B, T, width]} for every block with `kind`, from
+    `draws` draws (global indices draw_offset ..) scored against targets[layer] ([B, T, 512])."""
+    dev, B, T = w.device, cap.B, cap.T
+    rows = B * T
+    rope = w.rope(T)
+    per = max(1, min(draws, 1024, 65535 // B,
+                     max_workspace // max(1, int(_lib.load().noise_local_workspace_bytes(B, T, 1)))))
+    ws = workspace(dev, int(_lib.load().noise_local_workspace_bytes(B, T, per)))
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = {}
+    for layer in local_layers(kind):
+        li = inputs[layer] if inputs is not None and layer in inputs else LocalInputs(w, cap, layer)
+        target = targets[layer].reshape(rows, WIDTH).bfloat16().contiguous()
+        spec = li.spec(kind, target, sigma, gamma)
+        if kind in ('q', 'k'):
+            base = torch.empty(rows, 8, dtype=torch.float32, device=dev)
+            _lib.call('noise_local_baseline', _lib.ctypes.byref(spec), B, T, base.data_ptr(), status.data_ptr(),
+                      _stream(dev))
+            spec.base = base.data_ptr()
+        width = 8 if kind == 'gate' else WIDTH
+        err = torch.zeros(rows, width, dtype=torch.float32, device=dev)
+        for d0 in range(0, draws, per):
+            cnt = min(per, draws - d0)
+            _lib.call('noise_local_errors', _lib.ctypes.byref(spec), rope.data_ptr(), B, T, draw_offset + d0, cnt,
+                      seed & 0xFFFFFFFF, step & 0xFFFFFFFF, err.data_ptr(), ws.data_ptr(), ws.numel(),
+                      status.data_ptr(), _stream(dev))
+        if int(status.item()):
+            raise _lib.NoiseError('local errors: device wait timed out')
+        out[local_site(kind, layer)] = (err / draws).view(B, T, width)
+        del target
+    return out
+
+
+def reassemble_local(w: Weights, cap: Capture, kind: str, layer: int, error: torch.Tensor,
+                     inputs: LocalInputs | None = None) -> torch.Tensor:
+    """Weight gradient of a local site (run.py:465-471): value embeddings by token id, else err^T x."""
+    err = error.reshape(-1, error.shape[-1]).float()
+    if kind == 've':
+        g = torch.zeros(VOCAB, WIDTH, dtype=torch.float32, device=err.device)
+        return g.index_add_(0, cap.x.reshape(-1).long(), err)
+    li = inputs or LocalInputs(w, cap, layer)
+    return err.t() @ li.input_of(kind)
+
+
+# ------------------------------------------------------------------------------------------------
 # the estimator
 # ------------------------------------------------------------------------------------------------
 @dataclass
@@ -229,10 +345,10 @@ class DUST:
 
     Built here: capture, the coordinate head (head_error), direct errors of the writers, the MLP
     hidden layer, the embedding and the attention-output hubs (with the first block's reward-to-go),
-    reassembly, two-sided ES on the mixing scalars, the rank average with its finite check, and the
-    ANVIL II + AdamW step. Not built yet: the attention-internal local errors (q, k, v, gate, value
-    embeddings; run.py:391-463) and the credit-memory prior (run.py:281-330); those parameters keep a
-    zero estimate."""
+    the attention-internal local errors scored against the rank-averaged hubs, reassembly, two-sided
+    ES on the mixing scalars, the rank average with its finite check, and the ANVIL II + AdamW step.
+    Not built yet: the credit-memory prior (run.py:281-330), so every direct site runs without a
+    retrieval (the reference's first step)."""
 
     def __init__(self, w: Weights, rec: Recipe, seed: int = 0, rank: int = 0, world: int = 1):
         counts = rec.writers + rec.hidden + rec.hubs + [rec.embedding] + list(rec.local.values())
@@ -298,6 +414,14 @@ class DUST:
             sigma = 0.4 if layer < layers // 2 else 0.8
             gamma = r.first_gamma if layer == 0 else 0.0
             self.targets[layer] = self._average(self._errors([f'o@{layer}'], r.hubs[layer], sigma, layer, gamma)[f'o@{layer}'])
+        inputs = {layer: LocalInputs(self.w, cap, layer) for layer in range(layers)}
+        for kind, count in r.local.items():
+            per = count // self.world
+            errs = local_errors(self.w, cap, kind, per, self.targets, self.seed, self.t, draw_offset=self.rank * per,
+                                inputs=inputs)
+            for (name, err), layer in zip(errs.items(), local_layers(kind)):
+                grads.views[name + '.weight'].copy_(reassemble_local(self.w, cap, kind, layer, err, inputs[layer]))
+        del inputs
         for name, est in self.scalar_gradients(8 // self.world).items():
             grads.views[name].copy_(est)
         valid = (cap.y >= 0).sum().float()

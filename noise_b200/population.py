@@ -60,3 +60,18 @@ def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, m
         if code:
             raise _lib.NoiseError(f'population forward: device status {_lib.STATUS_NAMES.get(code, code)}')
     return out
+
+
+@torch.no_grad()
+def evaluate(weights: Weights, val: torch.Tensor, batch: int = 16) -> float:
+    """Mean next-token CE of the unperturbed model over validation rows [N, 2049] (utils/eval.py's
+    number, computed with sigma = 0 through the population forward)."""
+    total, count = 0.0, 0
+    for i in range(0, len(val), batch):
+        rows = val[i:i + batch].to(weights.device)
+        loss = population_losses(weights, rows[:, :-1], rows[:, 1:], 0, 1, 1, 0.0, 0, 0)
+        n = rows[:, 1:].numel()
+        total += float(loss.item()) * n
+        count += n
+    return total / count
+

@@ -33,8 +33,8 @@ def test_dust_step_pieces():
     from oracle import model as om
     w = Weights('cuda', seed=0)
     x, y = _batch()
-    rec = Recipe(writers=[32] * LAYERS, hidden=[32] * LAYERS, hubs=[32] * LAYERS, embedding=32, local={},
-                 nrep=16, lr=0.003)
+    rec = Recipe(writers=[32] * LAYERS, hidden=[32] * LAYERS, hubs=[32] * LAYERS, embedding=32,
+                 local=dict(q=16, v=16, gate=16, k=16, ve=16), nrep=16, lr=0.003)
     est = DUST(w, rec, seed=0)
     before = w.flat.clone()
     keep = _Keep()
@@ -47,8 +47,12 @@ def test_dust_step_pieces():
     cap = est.cap
     want = reassemble(cap, 'lm_head', head_error(cap)) / valid
     torch.testing.assert_close(g.views['lm_head.weight'], want, rtol=1e-5, atol=1e-8)
-    for name in ('transformer.wte.weight', 'transformer.h.3.mlp.c_fc.weight', 'transformer.h.0.attn.c_proj.weight'):
+    for name in ('transformer.wte.weight', 'transformer.h.3.mlp.c_fc.weight', 'transformer.h.0.attn.c_proj.weight',
+                 'transformer.h.2.attn.c_q.weight', 'transformer.h.5.attn.c_k.weight', 'transformer.h.7.attn.c_v.weight',
+                 'transformer.h.3.attn.ve_gate.weight', 'value_embeds.1.weight'):
         assert g.views[name].abs().sum() > 0, name
+    # every parameter has an estimate
+    assert all(v.abs().sum() > 0 for v in g.views.values())
 
     p = om.make_params(0)
     with torch.no_grad():
@@ -85,8 +89,8 @@ def test_dust_step_with_optimizers_lowers_loss():
     from noise_b200.optim import make_optimizer
     w = Weights('cuda', seed=0)
     x, y = _batch()
-    rec = Recipe(writers=[64] * LAYERS, hidden=[64] * LAYERS, hubs=[64] * LAYERS, embedding=64, local={},
-                 nrep=16, lr=0.003)
+    rec = Recipe(writers=[64] * LAYERS, hidden=[64] * LAYERS, hubs=[64] * LAYERS, embedding=64,
+                 local=dict(q=64, v=64, gate=64, k=64, ve=64), nrep=16, lr=0.003)
     est = DUST(w, rec, seed=0)
     opt = make_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 100)
     losses = [est.step(x, y, opt) for _ in range(4)]

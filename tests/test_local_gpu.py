@@ -1,0 +1,119 @@
+"""DUST's attention-internal errors on the GPU against the CPU oracle and the reference's fixtures
+(tests/golden/local.npz: DUST.local_errors with the same injected draws and seeded hub targets).
+
+Tolerances: processed queries within bf16 rounding (rel 1e-2 per element); clean scores relative L2
+2e-2 (bf16 q, k, values and P against fp32); the full estimate relative L2 <= 6e-2 and cosine >= 0.998
+against the reference: the GPU reruns carry bf16 operands where the CPU reference is fp32."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / 'golden'
+SEED, STEP = 0, 1
+KINDS = ['q', 'k', 'v', 'gate', 've']
+
+
+def _targets(b, t, layers=8, seed=21):
+    g = torch.Generator().manual_seed(seed)
+    return {i: torch.randn(b, t, 512, generator=g) * 0.01 for i in range(layers)}
+
+
+def _rel(got, want):
+    got, want = got.reshape(-1).double(), want.reshape(-1).double()
+    return ((got - want).norm() / want.norm()).item(), torch.nn.functional.cosine_similarity(got, want, dim=0).item()
+
+
+def _pick(f, key, flat):
+    """(ours, reference) over the entries the fixture keeps: all of a small array, else its samples."""
+    if key in f:
+        return flat, torch.from_numpy(f[key]).reshape(-1).double()
+    return flat[torch.from_numpy(f[key + '__idx'])], torch.from_numpy(f[key + '__val'])
+
+
+@pytest.fixture(scope='module')
+def golden():
+    return np.load(GOLDEN / 'local.npz')
+
+
+def _case(f, kind):
+    from noise_b200.data import zipf_tokens
+    from noise_b200.dust import Capture
+    from noise_b200.model import Weights
+    b, t, draws = (int(v) for v in f[f'le_{kind}_meta'])
+    rows = zipf_tokens(b, t + 1, seed=5)
+    x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+    w = Weights('cuda', seed=0)
+    return w, Capture(w, x, y), x, b, t, draws
+
+
+def test_processed_and_baseline_match_oracle(golden):
+    from noise_b200.dust import LocalInputs
+    from oracle import dust as od
+    from oracle import model as om
+    w, cap, x, b, t, _ = _case(golden, 'k')  # T = 1152: windows bind
+    p = om.make_params(0)
+    with torch.no_grad():
+        ocap = od.capture(p, x)
+    cos, sin = om.rotary_tables(t)
+    targets = _targets(b, t)
+    for layer in (0, 3, 5):
+        li = LocalInputs(w, cap, layer)
+        q, k, v, z, ve = od.attention_inputs(p, ocap, x, layer)
+        qp = om.rms_norm(om.rope(q, cos, sin))
+        got = li.processed['q'].float().cpu().view(b, t, 8, 64)
+        rel, cos_ = _rel(got, qp)
+        assert rel < 1e-2 and cos_ > 0.9999, (layer, rel, cos_)
+        # clean scores <target, attention(qp, kp, values)>
+        values = v if z is None else v + (2 * torch.sigmoid(z)).unsqueeze(-1) * ve
+        kp = om.rms_norm(om.rope(k, cos, sin))
+        att = om.window_attention(qp, kp, values, om.WINDOWS[layer])
+        want = torch.einsum('bthd,bthd->bth', targets[layer].view(b, t, 8, 64), att)
+        tgt = targets[layer].reshape(b * t, 512).cuda().bfloat16().contiguous()
+        spec = li.spec('q', tgt, 0.1, 0.98)
+        base = torch.empty(b * t, 8, device='cuda')
+        status = torch.zeros(1, dtype=torch.int32, device='cuda')
+        from noise_b200 import _lib
+        _lib.call('noise_local_baseline', _lib.ctypes.byref(spec), b, t, base.data_ptr(), status.data_ptr(),
+                  torch.cuda.current_stream().cuda_stream)
+        assert int(status.item()) == 0
+        rel, cos_ = _rel(base.cpu().view(b, t, 8), want)
+        print('baseline', layer, rel, cos_)
+        assert rel < 2e-2 and cos_ > 0.9998, (layer, rel, cos_)
+
+
+@pytest.mark.parametrize('kind', KINDS)
+def test_local_errors_match_reference(golden, kind):
+    from noise_b200.dust import LocalInputs, local_errors, local_layers, reassemble_local
+    f = golden
+    w, cap, x, b, t, draws = _case(f, kind)
+    targets = {i: v.cuda() for i, v in _targets(b, t).items()}
+    inputs = {i: LocalInputs(w, cap, i) for i in local_layers(kind)}
+    errs = local_errors(w, cap, kind, draws, targets, SEED, STEP, inputs=inputs)
+    for k, (site, e) in enumerate(errs.items()):
+        got, want = _pick(f, f'le_{kind}_{k}', e.cpu().double().reshape(-1))
+        rel, cos = _rel(got, want)
+        print(kind, site, 'rel', rel, 'cos', cos)
+        assert rel <= 6e-2 and cos >= 0.998, (site, rel, cos)
+    layer = local_layers(kind)[0]
+    site, e = next(iter(errs.items()))
+    g = reassemble_local(w, cap, kind, layer, e, inputs[layer]).cpu().double().reshape(-1)
+    rel, cos = _rel(*_pick(f, f'lr_{kind}', g))
+    print(kind, 'reassembled rel', rel, 'cos', cos)
+    assert rel <= 6e-2 and cos >= 0.998, (rel, cos)
+
+
+def test_local_errors_split_into_blocks_add_up(golden):
+    """Draw blocks are independent: one call over 32 draws equals two calls of 16 (same stream)."""
+    from noise_b200.dust import LocalInputs, local_errors
+    w, cap, x, b, t, _ = _case(golden, 'v')
+    targets = {i: v.cuda() for i, v in _targets(b, t).items()}
+    inputs = {i: LocalInputs(w, cap, i) for i in range(8)}
+    one = local_errors(w, cap, 'k', 32, targets, SEED, STEP, inputs=inputs)
+    lo = local_errors(w, cap, 'k', 16, targets, SEED, STEP, inputs=inputs)
+    hi = local_errors(w, cap, 'k', 16, targets, SEED, STEP, draw_offset=16, inputs=inputs)
+    for s in one:
+        torch.testing.assert_close(one[s], (lo[s] + hi[s]) / 2, rtol=1e-4, atol=1e-7)

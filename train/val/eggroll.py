@@ -19,37 +19,10 @@ import time
 import torch
 
 sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
-from noise_b200.data import zipf_tokens  # noqa: E402
+from noise_b200.data import ROW, TRAIN_ROWS, VAL_ROWS, load_rows  # noqa: E402
 from noise_b200.eggroll import BATCH, BETAS, CHUNK, LR, PAIRS, SEED, SIGMA, WARMDOWN, AdamW, Eggroll  # noqa: E402
 from noise_b200.model import Weights  # noqa: E402
-from noise_b200.population import population_losses  # noqa: E402
-
-TRAIN_ROWS, VAL_ROWS, ROW = 4880, 544, 2049  # utils/prepare_data.py:19-21 (rows of 2049 tokens)
-
-
-def load_rows(path: Path, rows: int, synthetic: bool, seed: int) -> torch.Tensor:
-    if path.exists():
-        data = torch.load(path)
-        if tuple(data.shape) != (rows, ROW):
-            raise ValueError(f'{path}: expected [{rows}, {ROW}], got {list(data.shape)}')
-        return data
-    if not synthetic:
-        raise FileNotFoundError(f'{path} is missing (prepare the data, or pass --synthetic)')
-    return zipf_tokens(rows, ROW, seed=seed)
-
-
-@torch.no_grad()
-def evaluate(weights: Weights, val: torch.Tensor, batch: int = 16) -> float:
-    """Mean next-token CE of the unperturbed model over the validation rows (sigma = 0)."""
-    total, count = 0.0, 0
-    for i in range(0, len(val), batch):
-        rows = val[i:i + batch].to(weights.device)
-        loss = population_losses(weights, rows[:, :-1], rows[:, 1:], 0, 1, 1, 0.0, 0, 0)
-        n = rows[:, 1:].numel()
-        total += float(loss.item()) * n
-        count += n
-    return total / count
-
+from noise_b200.population import evaluate  # noqa: E402
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
