@@ -2,7 +2,8 @@
 
 Reference: `train/val/run.py` — hadamard :143-152, orthogonal_noise :223-238, reward_to_go :81-86,
 head_loss :89-94, block_forward :102-117, coordinate_differences :120-137, rerun :256-279,
-direct_errors :332-378 (without the credit-memory prior), local_errors :391-463, reassemble :465-471.
+direct_errors :332-378 (with or without the credit-memory prior), local_errors :391-463, reassemble
+:465-471, and the credit memory :281-330 (memory_matrix, retrieve, remember, calibrate).
 
 Frames and signs of the orthogonal draws come from the counter-based stream (noise_b200's
 `csrc/dust.cuh` generates the same bits); parity with the reference is shown by injecting them into
@@ -116,9 +117,14 @@ def reward_to_go(reward: torch.Tensor, gamma: float) -> torch.Tensor:
     return out
 
 
-def direct_errors(clean_loss, perturbed, draws_by_site: dict, sigma: float, n: int, gamma: float = 0.0):
+def direct_errors(clean_loss, perturbed, draws_by_site: dict, sigma: float, n: int, gamma: float = 0.0,
+                  priors: dict | None = None):
     """Sum over chunks of n draws of -(centred reward) . a / sigma, divided by the draw count
-    (run.py:347-373 without the memory prior). perturbed [N, b, t]; draws_by_site[site] = a [N, b, t, d]."""
+    (run.py:347-378). perturbed [N, b, t]; draws_by_site[site] = a [N, b, t, d]. With priors
+    {site: mu [b, t, d]} (already masked like the draws), each reward gains the centred loss drop the
+    prior predicts, sigma sum_s a_s . mu_s, after the reward-to-go, and the estimate gains
+    (1 - 1/n) mu."""
+    priors = priors or {}
     total = perturbed.shape[0]
     errors = {s: torch.zeros(a.shape[1:], dtype=torch.float64) for s, a in draws_by_site.items()}
     for c0 in range(0, total, n):
@@ -127,9 +133,45 @@ def direct_errors(clean_loss, perturbed, draws_by_site: dict, sigma: float, n: i
             reward = reward - reward.mean(0, keepdim=True)
         if gamma:
             reward = reward_to_go(reward, gamma)
+        if priors:
+            predicted = sigma * sum(torch.einsum('nbtd,btd->nbt', draws_by_site[s][c0:c0 + n].double(), mu.double())
+                                    for s, mu in priors.items())
+            reward = reward + (predicted - predicted.mean(0, keepdim=True) if n > 1 else predicted)
         for s, a in draws_by_site.items():
             errors[s] -= torch.einsum('nbt,nbtd->btd', reward, a[c0:c0 + n].double()) / sigma
-    return {s: e / total for s, e in errors.items()}
+    kept = 1 - 1 / n if n > 1 else 1.0
+    return {s: e / total + kept * priors[s].double() if s in priors else e / total for s, e in errors.items()}
+
+
+def memory_matrix(S: torch.Tensor, P: torch.Tensor, ridge: float) -> torch.Tensor:
+    """M = S (P + ridge mean(diag P) I)^-1 through a Cholesky factor (run.py:281-292)."""
+    lam = ridge * P.diagonal().mean()
+    L = torch.linalg.cholesky(P + lam * torch.eye(len(P), dtype=P.dtype))
+    return torch.cholesky_solve(S.T, L).T
+
+
+def remember(P, S: dict, c: torch.Tensor, estimates: dict, valid, beta: float):
+    """EMA writes of the key covariance P and each site's S (run.py:304-314), single rank:
+    C = c^T c / valid, G = sum_t delta_t c_t^T / valid."""
+    cf = c.reshape(-1, c.shape[-1]).double()
+    C = cf.T @ cf / valid
+    P = beta * (P if P is not None else torch.zeros_like(C)) + (1 - beta) * C
+    out = {}
+    for site, e in estimates.items():
+        G = torch.einsum('btd,btk->dk', e.double(), c.double()) / valid
+        out[site] = beta * S.get(site, torch.zeros_like(G)) + (1 - beta) * G
+    return P, out
+
+
+def calibrate(calibration: dict, fits: dict, beta: float):
+    """alpha per site from EMAs of <r, estimate> and |r|^2 (run.py:316-330); returns (calibration, alpha)."""
+    cal, alpha = dict(calibration), {}
+    for site, (dot, ret) in fits.items():
+        if ret > 0:
+            od, orr = cal.get(site, (dot, ret))
+            cal[site] = (beta * od + (1 - beta) * dot, beta * orr + (1 - beta) * ret)
+            alpha[site] = cal[site][0] / cal[site][1]
+    return cal, alpha
 
 
 def block_forward(p: dict, i: int, x, ve, cos, sin, jitter: dict):

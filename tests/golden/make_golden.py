@@ -23,6 +23,9 @@ on CPU in float32 and saves their outputs as small .npz fixtures beside this scr
   local.npz        train/val/run.py DUST.local_errors for each kind (q, k, v, gate, ve) with injected
                    draws and seeded hub targets (LOCAL_CASES), plus the first block's reassembled
                    gradient per kind.
+  memory.npz       train/val/run.py credit memory: remember / memory_matrix / retrieve / calibrate on
+                   seeded estimates keyed by the real head error, and direct_errors with retrievals
+                   (MEMORY_SITES), sampled.
 
 Only the attention primitive is swapped, for the mathematically identical masked SDPA
 (`(q >= k) & (q - k <= window)`), because torch.compile(flex_attention) does not lower on CPU here;
@@ -75,6 +78,7 @@ def main():
     ap.add_argument('--only-dust', action='store_true')
     ap.add_argument('--only-optim', action='store_true')
     ap.add_argument('--only-local', action='store_true')
+    ap.add_argument('--only-memory', action='store_true')
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
     if args.only_dust:
@@ -85,6 +89,9 @@ def main():
         raise SystemExit
     if args.only_local:
         local_golden(args.reference)
+        raise SystemExit
+    if args.only_memory:
+        memory_golden(args.reference)
         raise SystemExit
     import utils.model as um
     import train.val.eggroll as eg
@@ -241,6 +248,75 @@ def local_golden(reference):
         out[f'le_{kind}_meta'] = np.array([b, t, draws])
         print('local', kind, {s: float(v.abs().mean()) for s, v in errs.items()})
     np.savez_compressed(HERE / 'local.npz', **pack(out, samples=1024))
+
+
+MEMORY_SITES = ['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj', 'transformer.h.6.mlp.c_fc', 'o@0']
+MEMORY_SEED = 31
+
+
+def memory_estimates(b: int, t: int, round_: int) -> dict:
+    """Seeded stand-ins for a step's site estimates, [b, t, d], 0.01 N(0, 1)."""
+    g = torch.Generator().manual_seed(MEMORY_SEED + round_)
+    width = {'transformer.h.6.mlp.c_fc': 2048}
+    return {s: torch.randn(b, t, width.get(s, 512), generator=g) * 0.01 for s in MEMORY_SITES}
+
+
+def memory_golden(reference):
+    """The credit memory (train/val/run.py:281-330) and direct_errors with its prior (:332-378): two
+    remember() writes of seeded estimates keyed by the real head error, the memory matrices and
+    retrievals, two calibrations, and direct_errors with retrievals for a writers group, an MLP hidden
+    site and a hub with reward-to-go."""
+    torch._dynamo.config.disable = True
+    import train.val.run as run
+    run.attention = sdpa_window
+    torch.set_num_threads(8)
+    model = run.make_model(torch.device('cpu'), SEED)
+    est = run.DUST(model, run.recipe(0.01), SEED, 0, 1)
+    rows = zipf_tokens(2, 129, seed=4)
+    x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
+    y[1, 5] = -1
+    b, t = x.shape
+    with torch.no_grad():
+        est.capture(x, y)
+        est.head_credit = est.head_error()[..., :4096]
+        valid = (y != -1).sum()
+        est.prior_sites = list(MEMORY_SITES)
+        out = {}
+        for round_ in range(2):
+            est.estimates = memory_estimates(b, t, round_)
+            est.remember(valid)
+        out['P'] = est.shared['P'].numpy()
+        for k, site in enumerate(MEMORY_SITES):
+            out[f'S_{k}'] = est.memory[site]['S'].numpy()
+            out[f'M_{k}'] = est.memory_matrix(site).numpy()
+        retrieved = est.retrieve(MEMORY_SITES)
+        for k, site in enumerate(MEMORY_SITES):
+            out[f'r_{k}'] = retrieved[site].numpy()
+        # calibration from two rounds of seeded fits
+        g = torch.Generator().manual_seed(MEMORY_SEED + 7)
+        for round_ in range(2):
+            est.fits = {s: torch.stack([torch.randn((), generator=g), torch.rand((), generator=g) + 0.5])
+                        for s in MEMORY_SITES}
+            out[f'fits_{round_}'] = torch.stack([est.fits[s] for s in MEMORY_SITES]).numpy()
+            est.calibrate()
+        out['alpha'] = np.array([est.alpha[s] for s in MEMORY_SITES])
+        # direct errors with the prior
+        est.orthogonal_noise = injector(run, est)
+        cases = [
+            ('writers', ['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj'], 32, 0.4, 1, 0.0),
+            ('hidden', ['transformer.h.6.mlp.c_fc'], 16, 0.4, 6, 0.0),
+            ('hub', ['o@0'], 16, 0.4, 0, 0.3),
+        ]
+        for name, sites, draws, sigma, entry, gamma in cases:
+            est.frames.clear()
+            est.fits.clear()
+            errs = est.direct_errors(sites, draws, sigma, entry, gamma, est.retrieve(sites))
+            for k, site in enumerate(sites):
+                out[f'pe_{name}_{k}'] = errs[site].numpy()
+                out[f'pf_{name}_{k}'] = est.fits[site].numpy()
+            out[f'pe_{name}_meta'] = np.array([draws, sigma, -1 if entry is None else entry, gamma])
+    np.savez_compressed(HERE / 'memory.npz', **pack(out, samples=1024))
+    print('memory', out['alpha'], {k: float(np.abs(v).mean()) for k, v in out.items() if k.startswith('pe_') and 'meta' not in k})
 
 
 def dust_golden(reference):
