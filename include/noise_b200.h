@@ -102,15 +102,25 @@ int noise_pop_capture(const float* params, const void* packed, const float* rope
                       const int32_t* targets, int B, int T, const NoiseCapture* out, void* workspace,
                       size_t workspace_bytes, int* status, void* stream);
 
-/* Replaces the contraction of DUST.direct_errors (train/val/run.py:347-368, without the memory
- * prior) for one site: with perturbed [draws][B*T] from noise_pop_forward_direct and clean [B*T],
- * rewards clean - perturbed are centred over chunks of `chunk` consecutive draws, optionally turned
- * into reward-to-go with decay gamma (run.py:81-86), and errors [B*T][d] -= sum_i reward_i a_i / sigma,
- * masked by live (bf16 [B*T][d] > 0) when given. draws <= 2048 per call; the caller divides by the
- * site's total draw count. */
+/* Credit-memory priors of the sites jittered together in one rerun (train/val/run.py:336-341): mu[s]
+ * is [B*T][d[s]] fp32, alpha * M c, masked like the site's draws. */
+typedef struct NoisePrior {
+  int count;            /* 0, 1 or 2 */
+  uint32_t site[2];     /* stream site ids of the draws */
+  int d[2];             /* widths (powers of two, <= 2048) */
+  const float* mu[2];
+} NoisePrior;
+
+/* Replaces the contraction of DUST.direct_errors (train/val/run.py:347-373) for one site: with
+ * perturbed [draws][B*T] from noise_pop_forward_direct and clean [B*T], rewards clean - perturbed are
+ * centred over chunks of `chunk` consecutive draws, optionally turned into reward-to-go with decay
+ * gamma (run.py:81-86), given the centred drop the priors predict (prior may be null), and
+ * errors [B*T][d] -= sum_i reward_i a_i / sigma, masked by live (bf16 [B*T][d] > 0) when given.
+ * draws <= 2048 per call; the caller divides by the site's total draw count and adds
+ * (1 - 1/chunk) mu for a site with a prior. */
 int noise_dust_errors(const float* clean, const float* perturbed, int draws, int chunk, int B, int T,
                       int64_t draw_begin, uint32_t site, int d, float sigma, float gamma, const void* live,
-                      uint32_t seed, uint32_t step, float* errors, void* stream);
+                      const NoisePrior* prior, uint32_t seed, uint32_t step, float* errors, void* stream);
 
 /* Replaces coordinate_differences (train/val/run.py:120-137): raw logits [rows][4096] -> the central
  * difference of each token's soft-capped CE along each of its logits, zero where targets < 0. */

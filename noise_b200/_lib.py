@@ -38,7 +38,7 @@ SIGNATURES: dict[str, tuple] = {
     'noise_pop_capture': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                   c_void_p, c_size_t, c_void_p, c_void_p]),
     'noise_dust_errors': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_uint32, c_int, c_float,
-                                  c_float, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+                                  c_float, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
     'noise_coordinate_differences': (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p, c_void_p]),
     'noise_local_process': (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     'noise_local_baseline': (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
@@ -73,6 +73,11 @@ class NoiseDirect(ctypes.Structure):
     """struct NoiseDirect of include/noise_b200.h."""
     _fields_ = [('entry', ctypes.c_int), ('mask', ctypes.c_uint32), ('site', ctypes.c_uint32 * 5),
                 ('sigma', ctypes.c_float), ('x_entry', c_void_p), ('inv0', c_void_p), ('live', c_void_p)]
+
+
+class NoisePrior(ctypes.Structure):
+    """struct NoisePrior of include/noise_b200.h."""
+    _fields_ = [('count', ctypes.c_int), ('site', ctypes.c_uint32 * 2), ('d', ctypes.c_int * 2), ('mu', c_void_p * 2)]
 
 
 class NoiseLocal(ctypes.Structure):

@@ -125,34 +125,142 @@ def rerun(w: Weights, cap: Capture, sites: list[Site], draws: int, draw_begin: i
     return out
 
 
+def prior_struct(sites: list[Site], priors: dict | None) -> _lib.NoisePrior | None:
+    """The NoisePrior of a rerun's jittered sites that carry a prior mu [B*T, d] (masked like the draws)."""
+    if not priors:
+        return None
+    p = _lib.NoisePrior()
+    for s in sites:
+        if s.name in priors:
+            mu = priors[s.name]
+            p.site[p.count], p.d[p.count], p.mu[p.count] = s.sid, s.width, mu.data_ptr()
+            p.count += 1
+    return p if p.count else None
+
+
 def accumulate_errors(cap: Capture, perturbed: torch.Tensor, s: Site, draw_begin: int, chunk: int, sigma: float,
-                      gamma: float, seed: int, step: int, errors: torch.Tensor | None = None) -> torch.Tensor:
-    """errors [B*T, d] -= sum_i centred reward_i a_i / sigma over the draws of `perturbed` (run.py:353-368)."""
+                      gamma: float, seed: int, step: int, errors: torch.Tensor | None = None,
+                      prior: _lib.NoisePrior | None = None) -> torch.Tensor:
+    """errors [B*T, d] -= sum_i centred reward_i a_i / sigma over the draws of `perturbed` (run.py:353-373)."""
     dev = perturbed.device
     if errors is None:
         errors = torch.zeros(cap.B * cap.T, s.width, dtype=torch.float32, device=dev)
     live = cap.hidden[s.layer].data_ptr() if s.kind == 3 else None
     _lib.call('noise_dust_errors', cap.clean_loss.data_ptr(), perturbed.data_ptr(), perturbed.shape[0], chunk, cap.B,
-              cap.T, draw_begin, s.sid, s.width, float(sigma), float(gamma), live, seed & 0xFFFFFFFF,
-              step & 0xFFFFFFFF, errors.data_ptr(), _stream(dev))
+              cap.T, draw_begin, s.sid, s.width, float(sigma), float(gamma), live,
+              _lib.ctypes.byref(prior) if prior is not None else None, seed & 0xFFFFFFFF, step & 0xFFFFFFFF,
+              errors.data_ptr(), _stream(dev))
     return errors
 
 
 def direct_errors(w: Weights, cap: Capture, names: list[str], draws: int, sigma: float, entry=None, gamma=0.0,
-                  seed: int = 0, step: int = 0, draw_offset: int = 0, nrep: int = 16) -> dict[str, torch.Tensor]:
-    """run.py:332-378 without the memory prior: per-site output errors [B, T, d] from `draws` direct
-    draws (global indices draw_offset ..), evaluated in blocks of whole chunks."""
+                  seed: int = 0, step: int = 0, draw_offset: int = 0, nrep: int = 16,
+                  priors: dict | None = None) -> dict[str, torch.Tensor]:
+    """run.py:332-378: per-site output errors [B, T, d] from `draws` direct draws (global indices
+    draw_offset ..), evaluated in blocks of whole chunks. priors {site: mu [B*T, d]} (alpha M c,
+    masked like the site's draws) make the draws estimate the residual around mu, which is added back
+    with centring's (1 - 1/n) shrinkage."""
     sites = [site(n) for n in names]
     n = chunk_size(draws, nrep)
     block = max(n, (2048 // n) * n)
+    priors = {k: v.reshape(cap.B * cap.T, -1).float().contiguous() for k, v in (priors or {}).items()}
+    pstruct = prior_struct(sites, priors)
     errors = {s.name: None for s in sites}
     for d0 in range(0, draws, block):
         cnt = min(block, draws - d0)
         perturbed = rerun(w, cap, sites, cnt, draw_offset + d0, sigma, entry, seed, step)
         for s in sites:
             errors[s.name] = accumulate_errors(cap, perturbed, s, draw_offset + d0, n, sigma, gamma, seed, step,
-                                               errors[s.name])
-    return {k: (v / draws).view(cap.B, cap.T, -1) for k, v in errors.items()}
+                                               errors[s.name], pstruct)
+    kept = 1 - 1 / n if n > 1 else 1.0
+    out = {}
+    for k, v in errors.items():
+        e = v / draws
+        if k in priors:
+            e = e + kept * priors[k]
+        out[k] = e.view(cap.B, cap.T, -1)
+    return out
+
+
+class CreditMemory:
+    """The credit memory of train/val/run.py:281-330: per direct site a ridge regression M = S (P +
+    ridge)^-1 from the head's output error c at a token to the site's own output error, with S and the
+    key covariance P kept as EMAs of this run's estimates, and a per-site scale alpha fitted on the
+    retrievals. Dense fp32 algebra in torch (cuBLAS GEMMs, one cuSOLVER Cholesky per step)."""
+
+    def __init__(self, beta: float = 0.9, ridge: float = 0.1, alpha_beta: float = 0.8, world: int = 1):
+        self.beta, self.ridge, self.alpha_beta, self.world = beta, ridge, alpha_beta, world
+        self.P = None
+        self.S, self.alpha, self.calibration, self.fits, self.estimates = {}, {}, {}, {}, {}
+        self._chol = None
+        self._chol_of = None
+
+    def _average(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+            t.div_(self.world)
+        return t
+
+    def matrix(self, name: str) -> torch.Tensor | None:
+        """M = S (P + ridge mean(diag P) I)^-1; one factorisation serves every site (run.py:281-292)."""
+        S = self.S.get(name)
+        if S is None:
+            return None
+        if self._chol_of is not self.P:
+            lam = self.ridge * self.P.diagonal().mean()
+            eye = torch.eye(len(self.P), dtype=self.P.dtype, device=self.P.device)
+            self._chol = torch.linalg.cholesky(self.P + lam * eye)
+            self._chol_of = self.P
+        return torch.cholesky_solve(S.T, self._chol).T
+
+    def retrieve(self, credit: torch.Tensor, names: list[str]) -> dict:
+        """{site: M c [B*T, d]} for the sites with a memory (run.py:294-302); credit is [B*T, 4096]."""
+        out = {}
+        for n in names:
+            M = self.matrix(n)
+            if M is not None:
+                out[n] = credit @ M.T
+        return out
+
+    def priors(self, retrieved: dict, live: dict | None = None) -> dict:
+        """alpha M c for the retrieved sites with a fitted alpha, masked by the live units (run.py:336-341)."""
+        out = {}
+        for n, r in retrieved.items():
+            if n in self.alpha:
+                mu = self.alpha[n] * r
+                if live and n in live:
+                    mu = mu * live[n]
+                out[n] = mu
+        return out
+
+    def fit(self, name: str, retrieved: torch.Tensor, estimate: torch.Tensor, kept: float):
+        """<r, estimate / kept> and |r|^2 for the next steps' alpha (run.py:375-377)."""
+        target = estimate.reshape(retrieved.shape) / kept
+        self.fits[name] = torch.stack([(retrieved * target).sum(), (retrieved * retrieved).sum()])
+
+    def calibrate(self):
+        """run.py:316-330: alpha = EMA<r, estimate> / EMA|r|^2 per site, fits averaged over ranks."""
+        names = list(self.fits)
+        if not names:
+            return
+        fits = self._average(torch.stack([self.fits[n] for n in names])).tolist()
+        for n, (dot, ret) in zip(names, fits):
+            if ret > 0:
+                od, orr = self.calibration.get(n, (dot, ret))
+                b = self.alpha_beta
+                self.calibration[n] = b * od + (1 - b) * dot, b * orr + (1 - b) * ret
+                self.alpha[n] = self.calibration[n][0] / self.calibration[n][1]
+        self.fits.clear()
+
+    def remember(self, credit: torch.Tensor, valid):
+        """run.py:304-314: P = EMA(c^T c / valid), S_site = EMA(sum_t estimate_t c_t^T / valid)."""
+        C = self._average(credit.T @ credit) / valid
+        self.P = C * (1 - self.beta) if self.P is None else self.beta * self.P + (1 - self.beta) * C
+        for n, e in self.estimates.items():
+            G = self._average(e.reshape(credit.shape[0], -1).T @ credit) / valid
+            S = self.S.get(n)
+            self.S[n] = G * (1 - self.beta) if S is None else self.beta * S + (1 - self.beta) * G
+        self.estimates.clear()
 
 
 def head_error(cap: Capture, sigma: float = 0.1) -> torch.Tensor:
@@ -343,12 +451,12 @@ def token_losses(w: Weights, cap: Capture) -> torch.Tensor:
 class DUST:
     """Forward-only gradient estimator of train/val/run.py:162-542 on noise_b200's kernels.
 
-    Built here: capture, the coordinate head (head_error), direct errors of the writers, the MLP
-    hidden layer, the embedding and the attention-output hubs (with the first block's reward-to-go),
-    the attention-internal local errors scored against the rank-averaged hubs, reassembly, two-sided
-    ES on the mixing scalars, the rank average with its finite check, and the ANVIL II + AdamW step.
-    Not built yet: the credit-memory prior (run.py:281-330), so every direct site runs without a
-    retrieval (the reference's first step)."""
+    Every phase of the reference's step: capture, the coordinate head (head_error, the memory's
+    key), direct errors of the writers, the MLP hidden layer, the embedding and the attention-output
+    hubs (the first block with reward-to-go) with the credit memory's priors, the attention-internal
+    local errors scored against the rank-averaged hubs, reassembly, two-sided ES on the mixing
+    scalars, calibration, the rank average with its finite check, the memory write, and the
+    ANVIL II + AdamW step."""
 
     def __init__(self, w: Weights, rec: Recipe, seed: int = 0, rank: int = 0, world: int = 1):
         counts = rec.writers + rec.hidden + rec.hubs + [rec.embedding] + list(rec.local.values())
@@ -357,11 +465,22 @@ class DUST:
         self.w, self.recipe, self.seed, self.rank, self.world = w, rec, seed, rank, world
         self.t = 0
         self.cap = None
+        self.memory = CreditMemory(rec.memory_beta, rec.mesa_ridge, rec.alpha_beta, world)
 
     def _errors(self, names, count, sigma, entry=None, gamma=0.0):
+        """direct_errors with the memory's retrievals (run.py:332-378); records fits and estimates."""
         per = count // self.world
-        return direct_errors(self.w, self.cap, names, per, sigma, entry, gamma, self.seed, self.t,
-                             draw_offset=self.rank * per, nrep=self.recipe.nrep)
+        retrieved = self.memory.retrieve(self.credit, names)
+        live = {n: (self.cap.hidden[entry] > 0).float() for n in names if n.endswith('mlp.c_fc')}
+        errs = direct_errors(self.w, self.cap, names, per, sigma, entry, gamma, self.seed, self.t,
+                             draw_offset=self.rank * per, nrep=self.recipe.nrep,
+                             priors=self.memory.priors(retrieved, live))
+        n = chunk_size(per, self.recipe.nrep)
+        kept = 1 - 1 / n if n > 1 else 1.0
+        for name, r in retrieved.items():
+            self.memory.fit(name, r, errs[name], kept)
+        self.memory.estimates.update(errs)
+        return errs
 
     def scalar_gradients(self, draws: int, sigma: float = 0.03) -> dict:
         """Two-sided ES for the 16 mixing scalars (run.py:473-491). The Gaussian directions come from
@@ -398,7 +517,8 @@ class DUST:
         r, layers = self.recipe, LAYERS
         self.cap = cap = Capture(self.w, x, y)
         grads = DenseGrad(self.w)
-        head = head_error(cap)
+        head = head_error(cap)  # the memory's key at each token
+        self.credit = head.view(-1, VOCAB)
         grads.views['lm_head.weight'].copy_(reassemble(cap, 'lm_head', head))
         for layer in range(layers):
             pre = f'transformer.h.{layer}.'
@@ -424,10 +544,12 @@ class DUST:
         del inputs
         for name, est in self.scalar_gradients(8 // self.world).items():
             grads.views[name].copy_(est)
+        self.memory.calibrate()  # the next step's alpha
         valid = (cap.y >= 0).sum().float()
         grads.flat.div_(valid)
         self._average(grads.flat)
         if not torch.isfinite(grads.flat).all():
             raise FloatingPointError('Non-finite estimate')
+        self.memory.remember(self.credit, valid)  # after this step's estimates
         optimizer.step(grads)
         return cap.clean_loss.view(cap.B, cap.T)[cap.y >= 0].mean().item()

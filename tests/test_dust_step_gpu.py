@@ -83,7 +83,8 @@ def test_dust_step_pieces():
 
 
 def test_dust_step_with_optimizers_lowers_loss():
-    """Three steps of DUST + ANVIL II/AdamW on one fixed batch lower its clean loss."""
+    """Four steps of DUST + ANVIL II/AdamW on one fixed batch lower its clean loss; the credit memory
+    holds every direct site and has fitted each prior's scale."""
     from noise_b200.dust import DUST, LAYERS, Recipe
     from noise_b200.model import Weights
     from noise_b200.optim import make_optimizer
@@ -94,6 +95,9 @@ def test_dust_step_with_optimizers_lowers_loss():
     est = DUST(w, rec, seed=0)
     opt = make_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 100)
     losses = [est.step(x, y, opt) for _ in range(4)]
-    print('losses', losses)
+    print('losses', losses, 'alpha', {k: round(v, 3) for k, v in est.memory.alpha.items()})
     assert all(torch.isfinite(torch.tensor(losses)))
     assert losses[-1] < losses[0], losses
+    # the credit memory is written every step and its priors are fitted after the second
+    assert est.memory.P is not None and len(est.memory.S) == 8 * 3 + 1 + 8
+    assert set(est.memory.alpha) == set(est.memory.S)
