@@ -34,6 +34,51 @@ struct WarpVecs {
   static constexpr int kBytes = 8 * kVecs * 128 * 4;
 };
 
+// Output staging for TMA stores: each epilogue warp owns two 4 KiB tiles of 32 rows x 128 bytes in the
+// 128-byte-swizzled layout of a {64 bf16, 32 rows} tensor-map box. A group's bf16 row segment is written
+// by its thread (16-byte chunk c of row r at position c ^ (r % 8): conflict-free), then lane 0 stores
+// the box with cp.async.bulk.tensor; a tile is rewritten only after the store issued from it two
+// groups earlier has read it.
+struct StoreStage {
+  static constexpr int kTileBytes = 32 * 128;
+  static constexpr int kBytes = 8 * 2 * kTileBytes + 1024;  // 8 warps x 2 tiles, plus alignment slack
+  uint8_t* tile[2];
+  int next = 0;
+  __device__ void init(uint8_t* region, int ew) {
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(region) + 1023) & ~uintptr_t(1023));
+    tile[0] = base + ew * 2 * kTileBytes;
+    tile[1] = tile[0] + kTileBytes;
+  }
+  // v[0..63] of row (row0 + lane) -> global columns [col, col + 64) through the map
+  __device__ void store64(const CUtensorMap* map, const float (&v)[64], int lane, int col, int row0) {
+    uint8_t* t = tile[next];
+    next ^= 1;
+    if (lane == 0) tma_store_wait_read<1>();
+    __syncwarp();
+    uint8_t* r = t + lane * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+      w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+      w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+      w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+      *reinterpret_cast<uint4*>(r + ((c ^ (lane & 7)) << 4)) = w;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, t, col, row0);
+      tma_store_commit();
+    }
+  }
+  // every store has completed (before the CTA's shared memory goes away)
+  __device__ void drain(int lane) {
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+};
+
 // Sum the kStatParts parts of a stats_a row into out[0..15].
 __device__ __forceinline__ void load_stats_a(const float* stats, int64_t row, float (&out)[16]) {
   const float* s = stats + (size_t)row * kStatParts * kStatStride;
@@ -54,6 +99,7 @@ __device__ __forceinline__ void load_stats_a(const float* stats, int64_t row, fl
 // ---------------------------------------------------------------------------------------------
 struct EpiQkv {
   struct Params {
+    CUtensorMap tm_qkv;     // qkv [rows, 1536] bf16, boxes of {64, 32}
     PopCtx ctx;
     __nv_bfloat16* qkv;     // [rows, 1536]
     const float* stats;     // stats_a
@@ -61,16 +107,19 @@ struct EpiQkv {
     const float* ve_table;  // [4096, 512] or nullptr
     int layer;
   };
-  static constexpr int kSmemBytes = WarpVecs<2>::kBytes;
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes + StoreStage::kBytes;
   static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // this warp's slots: [0] a of the tile's tensor, [1] b_ve
   int lane;
   RowInfo ri;
   float inv, xb[3], gate[kHeads], a_ve_tok;
+  StoreStage out;
 
   __device__ EpiQkv(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_) {
+    out.init(smem + WarpVecs<2>::kBytes, ew);
+  }
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
@@ -141,10 +190,11 @@ struct EpiQkv {
         for (int u = 0; u < 8; ++u) v[j + u] += g * (e[u] + sa * bve[j + u]);
       }
     }
-    st_bf16x64(p.qkv + (size_t)row * (3 * kWidth) + col, v);
+    out.store64(&p.tm_qkv, v, lane, col, row - lane);
   }
 
   __device__ void end_mtile(int, int, int) {}
+  __device__ void finish() { out.drain(lane); }
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -230,13 +280,14 @@ struct EpiProj {
 // ---------------------------------------------------------------------------------------------
 struct EpiFc {
   struct Params {
+    CUtensorMap tm_hidden;  // hidden [rows, 2048] bf16, boxes of {64, 32}
     PopCtx ctx;
     __nv_bfloat16* hidden;  // [rows, 2048]
     const float* stats;     // stats_b
     float* hstats;          // [rows][2] partial hidden.b_mlp
     int layer;
   };
-  static constexpr int kSmemBytes = WarpVecs<2>::kBytes;
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes + StoreStage::kBytes;
   static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // [0] a_fc, [1] b_mlp
@@ -245,9 +296,12 @@ struct EpiFc {
   float inv, c2, dmp;
   SiteJitter jit;  // direct mode: draw added to the live units' pre-activation (site 'fc')
   uint32_t patw[4];
+  StoreStage out;
 
   __device__ EpiFc(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {
+    out.init(smem + WarpVecs<2>::kBytes, ew);
+  }
 
   __device__ void begin_mtile(int, int row) {
     ri = row_info(p.ctx, row);
@@ -287,10 +341,11 @@ struct EpiFc {
       v[j] = bf16_round(r * r);
       dmp += v[j] * b[j];
     }
-    st_bf16x64(p.hidden + (size_t)row * kHidden + col, v);
+    out.store64(&p.tm_hidden, v, lane, col, row - lane);
   }
 
   __device__ void end_mtile(int, int, int row) { p.hstats[(size_t)row * 2 + half] = dmp; }
+  __device__ void finish() { out.drain(lane); }
 };
 
 // ---------------------------------------------------------------------------------------------

@@ -23,7 +23,11 @@
 //   __device__ void begin_tile(int m_tile, int n_tile, int col0)   warp-uniform; may __syncwarp
 //   __device__ void group(int row, int col, float (&v)[64])        64 consecutive columns of `row`
 //   __device__ void end_mtile(int m_tile, int n_tile, int row)     once per unit (n_tile = last one)
+// Optional:
+//   __device__ void finish()                                       once, after the last unit
 #pragma once
+
+#include <type_traits>
 
 #include "profile.cuh"
 #include "ptx.cuh"
@@ -53,6 +57,11 @@ struct TileUnit {
   }
   __host__ __device__ static int count(const GemmShape& s) { return kInterleaveN ? s.m_tiles * s.n_tiles : s.m_tiles; }
 };
+
+template <class E, class = void>
+struct HasFinish : std::false_type {};
+template <class E>
+struct HasFinish<E, std::void_t<decltype(&E::finish)>> : std::true_type {};
 
 template <int kStages>
 struct GemmLayout {
@@ -222,6 +231,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       }
       if (ok) epi.end_mtile(m, tu.n_end - 1, row);
     }
+    if constexpr (HasFinish<Epi>::value) epi.finish();
   }
 
   tc_fence_before();

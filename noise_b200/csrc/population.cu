@@ -325,7 +325,9 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
   }
   for (int l = first; l < kLayers; ++l) {
     const __nv_bfloat16* wl = packed + l * kPackLayer;
-    EpiQkv::Params q{ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
+    EpiQkv::Params q{{}, ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
+    if (make_tmap_2d(&q.tm_qkv, w.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, 32, 64))
+      return kStatusBadArgument;
     if ((rc = launch_gemm_tc<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
                                                   q, status, stream, kKindQkv)))
       return rc;
@@ -336,7 +338,9 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
                                                    status, stream, kKindProj)))
       return rc;
     if (cap && !copy(cap->mid + (size_t)l * rows * kWidth, w.x, rows * kWidth * 4)) return kStatusLaunchFailed;
-    EpiFc::Params fp{ctx, w.hidden, w.st_b, w.hstats, l};
+    EpiFc::Params fp{{}, ctx, w.hidden, w.st_b, w.hstats, l};
+    if (make_tmap_2d(&fp.tm_hidden, w.hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kHidden, kHidden, 32, 64))
+      return kStatusBadArgument;
     if ((rc = launch_gemm_tc<EpiFc, kGemmStages>(w.xb, wl + kPackFc, (int)rows, kHidden, kWidth, kWidth, kWidth, fp,
                                                  status, stream, kKindFc)))
       return rc;
