@@ -369,6 +369,7 @@ struct EpiMlpOut {
   };
   static constexpr int kSmemBytes = WarpVecs<6>::kBytes;
   static constexpr bool kInterleaveN = true;
+  static constexpr bool kPair = true;  // K = 2048: the 2-SM engine halves the weight traffic per MMA
   const Params& p;
   float* vec;  // [0] a_mlp, [1] b_wte, [2..4] next b_q, b_k, b_v (or [2] b_head), [5] next b_gate
   int lane, half;

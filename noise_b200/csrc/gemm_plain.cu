@@ -1,7 +1,7 @@
 // Plain GEMM through the tcgen05 engine: C = alpha * A * B^T, stored as fp32 or bf16. It has no
 // counterpart on the reference's path; it exists so the engine itself can be checked in isolation
 // (tests/test_gemm_gpu.py) before the fused epilogues are layered on it.
-#include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "noise_b200.h"
 
 namespace noise {
@@ -15,6 +15,7 @@ struct EpiStore {
   };
   static constexpr int kSmemBytes = 0;
   static constexpr bool kInterleaveN = false;
+  static constexpr bool kPair = true;
   const Params& p;
   __device__ EpiStore(const Params& p_, uint8_t*, int, int) : p(p_) {}
   __device__ void begin_mtile(int, int) {}
@@ -43,6 +44,6 @@ struct EpiStore {
 extern "C" int noise_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                                int out_bf16, int* status, void* stream) {
   noise::EpiStore::Params ep{C, N, alpha, out_bf16};
-  return noise::launch_gemm_tc<noise::EpiStore, 4>(A, B, M, N, K, K, K, ep, status,
+  return noise::launch_gemm<noise::EpiStore, 4>(A, B, M, N, K, K, K, ep, status,
                                                    reinterpret_cast<cudaStream_t>(stream), noise::kKindOther);
 }

@@ -15,6 +15,7 @@
 // direction, tensor).
 #include "attention_tc.cuh"
 #include "epilogues.cuh"
+#include "gemm_tc2.cuh"
 #include "noise_b200.h"
 
 namespace noise {
@@ -328,34 +329,34 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     EpiQkv::Params q{{}, ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
     if (make_tmap_2d(&q.tm_qkv, w.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, 32, 64))
       return kStatusBadArgument;
-    if ((rc = launch_gemm_tc<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
+    if ((rc = launch_gemm<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
                                                   q, status, stream, kKindQkv)))
       return rc;
     if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
     if (cap && !copy(cap->y + (size_t)l * rows * kWidth, w.y, rows * kWidth * 2)) return kStatusLaunchFailed;
     EpiProj::Params pp{ctx, w.x, w.xb, w.ystats, w.st_b, l};
-    if ((rc = launch_gemm_tc<EpiProj, kGemmStages>(w.y, wl + kPackProj, (int)rows, kWidth, kWidth, kWidth, kWidth, pp,
+    if ((rc = launch_gemm<EpiProj, kGemmStages>(w.y, wl + kPackProj, (int)rows, kWidth, kWidth, kWidth, kWidth, pp,
                                                    status, stream, kKindProj)))
       return rc;
     if (cap && !copy(cap->mid + (size_t)l * rows * kWidth, w.x, rows * kWidth * 4)) return kStatusLaunchFailed;
     EpiFc::Params fp{{}, ctx, w.hidden, w.st_b, w.hstats, l};
     if (make_tmap_2d(&fp.tm_hidden, w.hidden, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kHidden, kHidden, 32, 64))
       return kStatusBadArgument;
-    if ((rc = launch_gemm_tc<EpiFc, kGemmStages>(w.xb, wl + kPackFc, (int)rows, kHidden, kWidth, kWidth, kWidth, fp,
+    if ((rc = launch_gemm<EpiFc, kGemmStages>(w.xb, wl + kPackFc, (int)rows, kHidden, kWidth, kWidth, kWidth, fp,
                                                  status, stream, kKindFc)))
       return rc;
     if (cap && !copy(cap->hidden + (size_t)l * rows * kHidden, w.hidden, rows * kHidden * 2)) return kStatusLaunchFailed;
     const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
     EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next,
                          (cap && l == kLayers - 1) ? cap->final_x : nullptr, l};
-    if ((rc = launch_gemm_tc<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
+    if ((rc = launch_gemm<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
                                                      kHidden, mp, status, stream, kKindMlp)))
       return rc;
     if (cap && l + 1 < kLayers && !copy(cap->blocks + (size_t)(l + 1) * rows * kWidth, w.x, rows * kWidth * 4))
       return kStatusLaunchFailed;
   }
   EpiHead::Params hp{ctx, w.st_a, w.part, cap ? cap->logits : nullptr};
-  if ((rc = launch_gemm_tc<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
+  if ((rc = launch_gemm<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
                                                  hp, status, stream, kKindHead)))
     return rc;
   {
