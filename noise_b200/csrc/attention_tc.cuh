@@ -13,8 +13,9 @@
 // The groups run out of phase with each other, so the single MMA thread keeps the tensor core busy
 // while the special-function unit works through the exponentials.
 // Because q and k are unit-RMS, |q.k| / 8 <= 8 (up to bf16 rounding), so the softmax uses the fixed
-// offset 8: no running maximum and no rescaling of the TMEM accumulator. 32-key chunks outside a
-// warp's rows' windows skip their exponentials. TMEM: group g uses S at 128g and O at 128g + 64.
+// offset 8: no running maximum and no rescaling of the TMEM accumulator. Each query tile walks only
+// the key tiles its window reaches; 32-key chunks outside a warp's rows' windows skip their
+// exponentials. TMEM: group g uses S at 128g and O at 128g + 64.
 // Every wait is bounded (status word on timeout).
 //
 // Score mode (kScore, DUST's attention reruns, train/val/run.py:391-463): Q, K and V each come from
@@ -92,6 +93,10 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
   const int kt_begin = max(0, q0 - p.window) / kAtK;
   const int kt_end = (q0 + kAtQ * G - 1) / kAtK;
   const int n_kt = kt_end - kt_begin + 1;
+  // Each query tile g needs only key tiles [g_lo(g), g_hi(g)] of the CTA's range (relative indices):
+  // the tiles before its window are skipped by the MMA and softmax roles alike.
+  auto g_lo = [&](int g) { return max(0, q0 + kAtQ * g - p.window) / kAtK - kt_begin; };
+  auto g_hi = [&](int g) { return (q0 + kAtQ * g + kAtQ - 1) / kAtK - kt_begin; };
   int* status = p.status;
 
   if (tid == 0) {
@@ -166,7 +171,8 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
           tc_fence_after();
           const uint64_t dk = smem_desc_sw128(sK + st * kAtTileBytes);
           for (int g = 0; g < G && ok; ++g) {
-            if (!mbar_wait(&s_empty[g], (j & 1) ^ 1, abort_flag, status)) {
+            if (j < g_lo(g) || j > g_hi(g)) continue;
+            if (!mbar_wait(&s_empty[g], ((j - g_lo(g)) & 1) ^ 1, abort_flag, status)) {
               ok = false;
               break;
             }
@@ -182,7 +188,9 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
           const int jj = j - 1, st = jj % kAtStages;
           const uint64_t dv = smem_desc_sw128_mn(sV + st * kAtTileBytes);
           for (int g = 0; g < G && ok; ++g) {
-            if (!mbar_wait(&p_full[g], jj & 1, abort_flag, status)) {
+            const int lo = g_lo(g);
+            if (jj < lo || jj > g_hi(g)) continue;
+            if (!mbar_wait(&p_full[g], (jj - lo) & 1, abort_flag, status)) {
               ok = false;
               break;
             }
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
 #pragma unroll
             for (int k = 0; k < kAtK / 16; ++k)
               tc_mma_f16(tmem + 128 * g + 64, dp + 2 * k, dv + (uint64_t)(2048 >> 4) * k, idesc_o,
-                         (jj > 0 || k > 0) ? 1u : 0u);
+                         (jj > lo || k > 0) ? 1u : 0u);
             tc_commit(&p_empty[g]);
           }
           if (ok) tc_commit(&kv_empty[st]);
@@ -217,9 +225,11 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
     bool ok = true;
     uint8_t* prow = sP + g * kAtPBytes + r * 128;
     const int qlo = qg + quarter * 32, qhi = qlo + 31;  // this warp's rows
-    for (int j = 0; j < n_kt; ++j) {
+    const int j_lo = g_lo(g), j_hi = g_hi(g);
+    for (int j = j_lo; j <= j_hi; ++j) {
       const int k0 = (kt_begin + j) * kAtK;
-      if (!mbar_wait(&s_full[g], j & 1, abort_flag, status)) {
+      const uint32_t par = (uint32_t)(j - j_lo) & 1u;
+      if (!mbar_wait(&s_full[g], par, abort_flag, status)) {
         ok = false;
         break;
       }
@@ -229,7 +239,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G ==
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[g]);
-      if (!mbar_wait(&p_empty[g], (j & 1) ^ 1, abort_flag, status)) {
+      if (!mbar_wait(&p_empty[g], par ^ 1, abort_flag, status)) {
         ok = false;
         break;
       }
