@@ -3,7 +3,9 @@
 // RMS-normalised per head by the QKV epilogue.
 //
 // One CTA = G consecutive 128-query tiles x one head x one (member, sequence) row block. The G tiles
-// share every K/V tile the CTA streams. Warps:
+// share every K/V tile the CTA streams. The kernel is bound by the hand-offs between its roles, not
+// by the tensor or exp2 units, so it is sized for several independent CTAs per SM: G = 2, 96
+// registers, a 2-stage K/V ring (2 CTAs and 20 warps per SM; G = 1 when the tile count is odd). Warps:
 //   warp 0       TMA producer: the G Q tiles once, then 64-key K and V tiles into a 3-stage ring
 //   warp 1       TMEM owner and MMA issuer (one thread), per key tile j and query tile g:
 //                  S_g  = Q_g K_j^T    tcgen05.mma M=128 N=64 K=64, A and B K-major
@@ -44,7 +46,7 @@ struct AttnTcParams {
   int seqs;
 };
 
-constexpr int kAtQ = 128, kAtK = 64, kAtStages = 3;
+constexpr int kAtQ = 128, kAtK = 64, kAtStages = 2;
 constexpr int kAtTileBytes = kAtK * kHeadDim * 2;  // 8 KB: 64 rows x 128 B
 constexpr int kAtQBytes = kAtQ * kHeadDim * 2;     // 16 KB
 constexpr int kAtPBytes = kAtQ * kAtK * 2;         // 16 KB
@@ -58,7 +60,7 @@ struct AttnTcLayout {
 };
 
 template <int G, bool kScore>
-__global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, 1) __maxnreg__(G == 4 ? 112 : 168)
+__global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnTcParams p) {
   using L = AttnTcLayout<G>;

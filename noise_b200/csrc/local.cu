@@ -288,7 +288,6 @@ int launch_local_attention(const NoiseLocal* s, int B, int T, int Z, const __nv_
   ap.target = reinterpret_cast<const __nv_bfloat16*>(s->target);
   ap.base = base, ap.score = score, ap.seqs = B;
   const int n_qt = T / kAtQ;
-  if (n_qt % 4 == 0) return launch_local_attention_g<4>(tm[0], tm[1], tm[2], ap, Z, stream);
   if (n_qt % 2 == 0) return launch_local_attention_g<2>(tm[0], tm[1], tm[2], ap, Z, stream);
   return launch_local_attention_g<1>(tm[0], tm[1], tm[2], ap, Z, stream);
 }

@@ -279,8 +279,7 @@ int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& 
   ap.ctx = ctx, ap.y = w.y, ap.ystats = w.ystats, ap.layer = layer, ap.window = layer_window(layer);
   ap.status = status;
   ap.col_q = 0, ap.col_k = kWidth, ap.col_v = 2 * kWidth;
-  const int n_qt = ctx.T / kAtQ;  // query tiles per sequence; a CTA takes 4, 2 or 1 of them
-  if (n_qt % 4 == 0) return launch_attention_g<4>(tm, ap, rows, stream);
+  const int n_qt = ctx.T / kAtQ;  // query tiles per sequence; a CTA takes 2 or 1 of them
   if (n_qt % 2 == 0) return launch_attention_g<2>(tm, ap, rows, stream);
   return launch_attention_g<1>(tm, ap, rows, stream);
 }
