@@ -46,30 +46,38 @@ struct AttnTcParams {
   int seqs;
 };
 
-constexpr int kAtQ = 128, kAtK = 64, kAtStages = 2;
-constexpr int kAtTileBytes = kAtK * kHeadDim * 2;  // 8 KB: 64 rows x 128 B
-constexpr int kAtQBytes = kAtQ * kHeadDim * 2;     // 16 KB
-constexpr int kAtPBytes = kAtQ * kAtK * 2;         // 16 KB
+constexpr int kAtQ = 128, kAtStages = 2;
+constexpr int kAtQBytes = kAtQ * kHeadDim * 2;  // 16 KB
 
-template <int G>
+// G query tiles per CTA, key tiles of KT keys (64 or 128). A K or V tile is KT rows x 128 B; P is KT / 64
+// swizzled sub-tiles of 128 rows x 64 keys per query tile. TMEM per query tile: S (KT columns), then O.
+template <int G, int KT>
 struct AttnTcLayout {
   static constexpr int kThreads = (2 + 4 * G) * 32;
-  static constexpr int kCore = G * kAtQBytes + 2 * kAtStages * kAtTileBytes + G * kAtPBytes;
-  static constexpr int kSmem = 1024 + kCore + 512 + kHeadDim * 4;
-  static constexpr uint32_t kTmemCols = 128 * G;
+  static constexpr int kTileBytes = KT * kHeadDim * 2;
+  static constexpr int kPBytes = kAtQ * KT * 2;
+  static constexpr int kCore = G * kAtQBytes + 2 * kAtStages * kTileBytes + G * kPBytes;
+  // 128-key tiles fit two CTAs per SM only without the alignment slack: the kernel then checks that
+  // the dynamic shared base is 1024-aligned (it follows the per-CTA reserved kilobyte)
+  static constexpr int kSlack = KT == 64 ? 1024 : 0;
+  static constexpr int kSmem = kSlack + kCore + 512 + kHeadDim * 4;
+  static constexpr uint32_t kGroupCols = KT == 64 ? 128 : 256;
+  static constexpr uint32_t kTmemCols = kGroupCols * G;
 };
 
-template <int G, bool kScore>
-__global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
+template <int G, int KT, bool kScore>
+__global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT == 64 ? 3 : 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnTcParams p) {
-  using L = AttnTcLayout<G>;
+  using L = AttnTcLayout<G, KT>;
+  constexpr int kAtK = KT, kAtTileBytes = L::kTileBytes, kAtPBytes = L::kPBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const bool misaligned = L::kSlack == 0 && base != smem_raw;
   uint8_t* sQ = base;                              // [g] 16 KB
-  uint8_t* sK = sQ + G * kAtQBytes;                // [stage] 8 KB
-  uint8_t* sV = sK + kAtStages * kAtTileBytes;     // [stage] 8 KB
-  uint8_t* sP = sV + kAtStages * kAtTileBytes;     // [g] 16 KB
+  uint8_t* sK = sQ + G * kAtQBytes;                // [stage] KT x 128 B
+  uint8_t* sV = sK + kAtStages * kAtTileBytes;     // [stage] KT x 128 B
+  uint8_t* sP = sV + kAtStages * kAtTileBytes;     // [g] KT / 64 sub-tiles of 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kCore);
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;            // [kAtStages]
@@ -94,7 +102,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
   const int q0 = unit * kAtQ * G;  // first query of the CTA
   const int kt_begin = max(0, q0 - p.window) / kAtK;
   const int kt_end = (q0 + kAtQ * G - 1) / kAtK;
-  const int n_kt = kt_end - kt_begin + 1;
+  const int n_kt = misaligned ? 0 : kt_end - kt_begin + 1;
   // Each query tile g needs only key tiles [g_lo(g), g_hi(g)] of the CTA's range (relative indices):
   // the tiles before its window are skipped by the MMA and softmax roles alike.
   auto g_lo = [&](int g) { return max(0, q0 + kAtQ * g - p.window) / kAtK - kt_begin; };
@@ -112,7 +120,8 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
     }
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    *abort_flag = misaligned ? 1 : 0;
+    if (misaligned) atomicExch(p.status, kStatusUnsupported);
     fence_mbarrier_init();
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
@@ -138,21 +147,25 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       const int64_t rq = operand_rows(p.mod_q), rk = operand_rows(p.mod_k), rv = operand_rows(p.mod_v);
-      mbar_arrive_expect_tx(q_full, G * kAtQBytes);
-      for (int b = 0; b < 2 * G; ++b)
-        tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_q, q_full, qcol, (int)(rq + q0 + 64 * b));
+      if (!misaligned) {
+        mbar_arrive_expect_tx(q_full, G * kAtQBytes);
+        for (int b = 0; b < 2 * G; ++b)
+          tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_q, q_full, qcol, (int)(rq + q0 + 64 * b));
+      }
       int issued = 0;
       for (int j = 0; j < n_kt; ++j) {
         const int st = j % kAtStages;
         if (!mbar_wait(&kv_empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, status)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kAtTileBytes);
         const int r = (kt_begin + j) * kAtK;
-        tma_load_2d(sK + st * kAtTileBytes, &tm_k, &kv_full[st], kcol, (int)(rk + r));
-        tma_load_2d(sV + st * kAtTileBytes, &tm_v, &kv_full[st], vcol, (int)(rv + r));
+        for (int h = 0; h < KT / 64; ++h) {  // boxes of 64 rows
+          tma_load_2d(sK + st * kAtTileBytes + h * 8192, &tm_k, &kv_full[st], kcol, (int)(rk + r + 64 * h));
+          tma_load_2d(sV + st * kAtTileBytes + h * 8192, &tm_v, &kv_full[st], vcol, (int)(rv + r + 64 * h));
+        }
         issued = j + 1;
       }
       // copies in flight land before the CTA can exit
-      mbar_wait(q_full, 0, abort_flag, status);
+      if (!misaligned) mbar_wait(q_full, 0, abort_flag, status);
       for (int j = max(0, issued - kAtStages); j < issued; ++j)
         mbar_wait(&kv_full[j % kAtStages], (j / kAtStages) & 1, abort_flag, status);
     }
@@ -182,7 +195,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
             const uint64_t dq = smem_desc_sw128(sQ + g * kAtQBytes);
 #pragma unroll
             for (int k = 0; k < kHeadDim / 16; ++k)
-              tc_mma_f16(tmem + 128 * g, dq + 2 * k, dk + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+              tc_mma_f16(tmem + L::kGroupCols * g, dq + 2 * k, dk + 2 * k, idesc_s, k > 0 ? 1u : 0u);
             tc_commit(&s_full[g]);
           }
         }
@@ -197,11 +210,12 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
               break;
             }
             tc_fence_after();
-            const uint64_t dp = smem_desc_sw128(sP + g * kAtPBytes);
 #pragma unroll
-            for (int k = 0; k < kAtK / 16; ++k)
-              tc_mma_f16(tmem + 128 * g + 64, dp + 2 * k, dv + (uint64_t)(2048 >> 4) * k, idesc_o,
+            for (int k = 0; k < kAtK / 16; ++k) {
+              const uint64_t dp = smem_desc_sw128(sP + g * kAtPBytes + (k >> 2) * 16384);
+              tc_mma_f16(tmem + L::kGroupCols * g + KT, dp + 2 * (k & 3), dv + (uint64_t)(2048 >> 4) * k, idesc_o,
                          (jj > lo || k > 0) ? 1u : 0u);
+            }
             tc_commit(&p_empty[g]);
           }
           if (ok) tc_commit(&kv_empty[st]);
@@ -220,7 +234,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
     const int qg = q0 + kAtQ * g;           // first query of tile g
     const int q = qg + r;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tmem + 128 * g, tO = tS + 64;
+    const uint32_t tS = tmem + L::kGroupCols * g, tO = tS + KT;
     const float kScaleLog2 = 0.125f * 1.4426950408889634f;
     const float kOffsetLog2 = 8.0f * 1.4426950408889634f;
     float lsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
@@ -236,18 +250,23 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
         break;
       }
       tc_fence_after();
+#pragma unroll 1
+      for (int h = 0; h < KT / 64; ++h) {  // 64-key halves of S, each into its own P sub-tile
       float sv[64];
-      tmem_ld64(tS + lane_addr, sv);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[g]);
-      if (!mbar_wait(&p_empty[g], par ^ 1, abort_flag, status)) {
+      tmem_ld64(tS + lane_addr + 64 * h, sv);
+      if (h == KT / 64 - 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[g]);
+      }
+      if (h == 0 && !mbar_wait(&p_empty[g], par ^ 1, abort_flag, status)) {
         ok = false;
         break;
       }
+      uint8_t* ph = prow + h * 16384;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        const int kc = k0 + 32 * c;
+        const int kc = k0 + 64 * h + 32 * c;
         // warp-uniform classification of the 32 x 32 block (this warp's rows x the chunk's keys)
         const bool none = kc > qhi || qlo - (kc + 31) > p.window;
         const bool all = (kc + 31 <= qlo) && (qhi - kc <= p.window);
@@ -270,9 +289,11 @@ __global__ void __launch_bounds__(AttnTcLayout<G>::kThreads, G == 1 ? 3 : 2)
             }
           }
           // P row r: chunk (4c + b) stored at (4c + b) ^ (r % 8) (128-byte swizzle)
-          *reinterpret_cast<uint4*>(prow + (((4 * c + b) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(ph + (((4 * c + b) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      }
+      if (!ok) break;
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g]);

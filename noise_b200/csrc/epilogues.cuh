@@ -72,6 +72,23 @@ struct StoreStage {
       tma_store_commit();
     }
   }
+  // the same with the 64 values already packed to bf16 pairs
+  __device__ void store64_packed(const CUtensorMap* map, const uint32_t (&w)[32], int lane, int col, int row0) {
+    uint8_t* t = tile[next];
+    next ^= 1;
+    if (lane == 0) tma_store_wait_read<1>();
+    __syncwarp();
+    uint8_t* r = t + lane * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(r + ((c ^ (lane & 7)) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, t, col, row0);
+      tma_store_commit();
+    }
+  }
   // every store has completed (before the CTA's shared memory goes away)
   __device__ void drain(int lane) {
     if (lane == 0) tma_store_wait_all<0>();
@@ -324,24 +341,33 @@ struct EpiFc {
   __device__ void group(int row, int col, float (&v)[64]) {
     const float* a = vec + (col & 127);
     const float* b = vec + 128 + (col & 127);
-#pragma unroll
-    for (int j = 0; j < 64; ++j) v[j] = inv * (v[j] + c2 * a[j]);
-    if (jit.on) {
+    if (jit.on) {  // direct mode: the draw joins the normalised pre-activation of live units
       const int64_t seq_rows = (int64_t)p.ctx.B * p.ctx.T;
       const __nv_bfloat16* lv = p.ctx.dir.live + (size_t)(row % seq_rows) * kHidden + col;
 #pragma unroll
-      for (int j = 0; j < 64; ++j)
-        if (__bfloat162float(lv[j]) > 0.f)
-          v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
-    }
+      for (int j = 0; j < 64; ++j) {
+        v[j] = inv * (v[j] + c2 * a[j]);
+        if (__bfloat162float(lv[j]) > 0.f) v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
+        const float r = fmaxf(v[j], 0.f);
+        v[j] = r * r;
+      }
+    } else {
+      // relu(inv (x + c2 a))^2 = inv^2 relu(x + c2 a)^2 for inv > 0
+      const float inv2 = inv * inv;
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const float pre = v[j];
-      const float r = fmaxf(pre, 0.f);
-      v[j] = bf16_round(r * r);
-      dmp += v[j] * b[j];
+      for (int j = 0; j < 64; ++j) {
+        const float r = fmaxf(v[j] + c2 * a[j], 0.f);
+        v[j] = (r * r) * inv2;
+      }
     }
-    out.store64(&p.tm_hidden, v, lane, col, row - lane);
+    // bf16 hidden once; its statistic hidden . b_mlp is taken from the rounded values
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      dmp += __uint_as_float(w[i] << 16) * b[2 * i] + __uint_as_float(w[i] & 0xFFFF0000u) * b[2 * i + 1];
+    }
+    out.store64_packed(&p.tm_hidden, w, lane, col, row - lane);
   }
 
   __device__ void end_mtile(int, int, int row) { p.hstats[(size_t)row * 2 + half] = dmp; }

@@ -247,20 +247,22 @@ __global__ void __launch_bounds__(256) local_contract_kernel(const __grid_consta
   }
 }
 
-template <int G>
+constexpr int kLocalKeyTile = 64;  // as the population forward's attention (population.cu)
+
+template <int G, int KT>
 int launch_local_attention_g(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const AttnTcParams& ap, int Z, cudaStream_t stream) {
-  using L = AttnTcLayout<G>;
+  using L = AttnTcLayout<G, KT>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attention_tc_kernel<G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
+    if (cudaFuncSetAttribute(attention_tc_kernel<G, KT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
         cudaSuccess)
       return kStatusLaunchFailed;
     configured = true;
   }
   dim3 grid(ap.ctx.T / (kAtQ * G), kHeads, (unsigned)Z);
   LaunchScope scope(kKindAttention, stream);
-  attention_tc_kernel<G, true><<<grid, L::kThreads, L::kSmem, stream>>>(tq, tk, tv, ap);
+  attention_tc_kernel<G, KT, true><<<grid, L::kThreads, L::kSmem, stream>>>(tq, tk, tv, ap);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
 
@@ -288,8 +290,9 @@ int launch_local_attention(const NoiseLocal* s, int B, int T, int Z, const __nv_
   ap.target = reinterpret_cast<const __nv_bfloat16*>(s->target);
   ap.base = base, ap.score = score, ap.seqs = B;
   const int n_qt = T / kAtQ;
-  if (n_qt % 2 == 0) return launch_local_attention_g<2>(tm[0], tm[1], tm[2], ap, Z, stream);
-  return launch_local_attention_g<1>(tm[0], tm[1], tm[2], ap, Z, stream);
+  if (kLocalKeyTile == 128) return launch_local_attention_g<1, 128>(tm[0], tm[1], tm[2], ap, Z, stream);
+  if (n_qt % 2 == 0) return launch_local_attention_g<2, 64>(tm[0], tm[1], tm[2], ap, Z, stream);
+  return launch_local_attention_g<1, 64>(tm[0], tm[1], tm[2], ap, Z, stream);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
