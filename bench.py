@@ -270,7 +270,8 @@ def main():
     roofline = {
         'bound': 'tensor', 'kernel': dominant, 'achieved': achieved, 'peak': peak_sustained, 'unit': 'TFLOP/s',
         'frac': achieved / peak_sustained, 'peak_source': f'{peak_kind} bf16_tflops_sustained',
-        'traffic': TRAFFIC_PER_LAUNCH.get(dominant),
+        'traffic': (TRAFFIC_BYTES_PER_ROW[dominant] * local_tokens * (1 if dominant == 'head' else 8)
+                    / max(1, kind_n[dominant])) if dominant in TRAFFIC_BYTES_PER_ROW else None,
         'launches': kind_n[dominant], 'ms_per_launch': kind_ms[dominant] / max(1, kind_n[dominant]),
         'population_forward': {'achieved': fwd_tflops, 'frac': fwd_tflops / peak_sustained,
                                'frac_of_burst': fwd_tflops / peak_burst},
@@ -302,8 +303,10 @@ def main():
         torch.distributed.destroy_process_group()
 
 
-# dram bytes per launch of each kind from ncu captures (profiles/), scaled to the bench's launch size
-TRAFFIC_PER_LAUNCH: dict = {}
+# DRAM bytes (read + write) per population row of one launch of each kind, from one ncu capture of the
+# small case (profiles/gemm_attention_small_1xb200.md: 262,144 rows per launch); traffic grows in
+# proportion to the rows, so a bench launch's traffic is this times its rows.
+TRAFFIC_BYTES_PER_ROW = {'attention': 4089, 'qkv': 4219, 'proj': 6101, 'fc': 5057, 'mlp': 10166}
 
 
 def ctypes_array(code, n):
