@@ -8,6 +8,7 @@ reconstruction fused with AdamW (lr 1e-3), packed-weight refresh.
 
     python bench.py [--gpus N --steps K --warmup W]          # this repository's CUDA path
     python bench.py --impl reference [...]                   # the CPU restatement of the reference path
+    python bench.py --workload dust [--dust-scale S]          # seconds per DUST update (a separate line)
 Multi-GPU: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
 Rank 0 prints one JSON line.
 """
@@ -172,10 +173,16 @@ def main():
     ap.add_argument('--sigma', type=float, default=1e-3)
     ap.add_argument('--workspace-gb', type=float, default=32.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--workload', default='eggroll', choices=['eggroll', 'dust'],
+                    help='eggroll (the headline line) or dust: seconds per DUST update, a separate line')
+    ap.add_argument('--dust-scale', type=float, default=0.3125, help='DUST recipe scale (1.0 = the 16k cell)')
     args = ap.parse_args()
     rank, world, local = dist_setup()
     if args.impl == 'reference':
         run_reference(args, rank, world)
+        return
+    if args.workload == 'dust':
+        run_dust(args, rank, world, local)
         return
 
     from noise_b200 import _lib, population
@@ -301,6 +308,78 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+# The reference's own logs on 8xH100 (train/val/log, train/speedrun/log): seconds per DUST update.
+DUST_PUBLISHED_8XH100 = {1.0: 4303.45 / 610, 0.3125: 1309.72 / 610}
+
+
+def run_dust(args, rank, world, local):
+    """Seconds per DUST update (train/val/run.py DUST.step + ANVIL II / AdamW) on B = 8 sequences of
+    2048 tokens, inputs copied from pinned host memory every step; the recipe's draws split over the
+    GPUs (strong scaling, as the reference)."""
+    from noise_b200 import _lib
+    from noise_b200.data import zipf_tokens
+    from noise_b200.dust import DUST, recipe
+    from noise_b200.model import Weights
+    from noise_b200.optim import make_optimizer
+
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=600), device_id=dev)
+    lib = _lib.load()
+    rec = recipe(args.dust_scale)
+    w = Weights(dev, seed=0)
+    est = DUST(w, rec, 0, rank, world)
+    opt = make_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 610)
+    rows = zipf_tokens(BATCH, SEQ + 1, seed=1).pin_memory()
+    x, y = rows[:, :-1], rows[:, 1:]
+    for _ in range(args.warmup):
+        est.step(x, y, opt)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream(dev)
+    launches0 = lib.noise_launch_count()
+    _lib.call('noise_profile_enable', 1)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            loss = est.step(x, y, opt)  # reads the clean loss back to the host
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = lib.noise_launch_count() - launches0
+    ms_kind = (ctypes_array('d', len(KINDS)), ctypes_array('q', len(KINDS)))
+    _lib.call('noise_profile_read', ms_kind[0].buffer_info()[0], ms_kind[1].buffer_info()[0], len(KINDS))
+    _lib.call('noise_profile_enable', 0)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    published = DUST_PUBLISHED_8XH100.get(args.dust_scale)
+    clk = clocks.summary()
+    draws = sum(rec.writers) + sum(rec.hidden) + sum(rec.hubs) + rec.embedding + sum(rec.local.values())
+    line = {
+        'metric': 'seconds per DUST update (B = 8 x 2048 tokens)', 'value': ms / 1e3, 'unit': 's',
+        'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': False,
+        'scaling': 'strong', 'vs_baseline': (ms / 1e3) / published if (published and world == 8) else None,
+        'dtype': 'bf16', 'data': 'synthetic Zipf(1.1) tokens, seed-0 random init (FineWeb unavailable offline)',
+        'config': {'workload': f'dust-recipe-{args.dust_scale}', 'draws_per_update': draws,
+                   'optimizer': 'ANVIL II on block matrices, AdamW elsewhere',
+                   'reference_8xh100_s_per_update': published, 'last_clean_loss': loss},
+        'e2e': {'value': ms / 1e3, 'unit': 's', 'h2d_bytes_per_step': rows.numel() * rows.element_size(),
+                'd2h_bytes_per_step': 4},
+        'gpu_launches': launches,
+        'kernel_ms_per_step': {k: round(ms_kind[0][i] / args.steps, 3) for i, k in enumerate(KINDS) if ms_kind[1][i]},
+        'clocks': {'sm_mhz': clk['sm_mhz'], 'sm_max_mhz': clk['sm_max_mhz'], 'reasons': clk['reasons']},
+    }
+    print(json.dumps(line), flush=True)
 
 
 # DRAM bytes (read + write) per population row of one launch of each kind, from one ncu capture of the
