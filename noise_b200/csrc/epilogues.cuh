@@ -581,13 +581,19 @@ struct EpiHead {
 #pragma unroll
       for (int j = 0; j < 64; j += 8) st_global_v8f(p.logits + (size_t)row * kVocab + col + j, lg + j);
     }
+    // exp(z - 15) with z = 15 tanh(l / 15): since tanh(u) - 1 = -2 / (e^(2u) + 1),
+    // z - 15 = -30 / (e^(2 l / 15) + 1), i.e. two base-2 exponentials and one reciprocal per logit.
+    const float k_in = 2.0f / kSoftCap * 1.4426950408889634f;
+    const float k_out = -2.0f * kSoftCap * 1.4426950408889634f;
+    float lt = 0.f;
+    bool mine = false;
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
       const float logit = inv * (v[j] + c2 * a[j]);
-      const float z = kSoftCap * tanhf(logit * (1.0f / kSoftCap));
-      se += expf(z - kSoftCap);
-      if (col + j == ri.tgt) zt = z;
+      se += ex2_approx(k_out * rcp_approx(ex2_approx(logit * k_in) + 1.0f));
+      if (col + j == ri.tgt) lt = logit, mine = true;
     }
+    if (mine) zt = kSoftCap * tanhf(lt * (1.0f / kSoftCap));  // the target's capped logit, once per row
   }
 
   __device__ void end_mtile(int, int, int row) {

@@ -401,6 +401,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 1/x on the special-function unit (one MUFU.RCP, flush-to-zero; ~1 ulp)
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
