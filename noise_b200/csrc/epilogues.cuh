@@ -96,6 +96,61 @@ struct StoreStage {
   }
 };
 
+// Input staging for the fp32 residual rows an epilogue reads: each epilogue warp owns one 8 KiB tile
+// of 32 rows x 64 floats, filled by two {32 fp32, 32 rows} tensor-map boxes (128-byte swizzle: the
+// 16-byte chunk c of row r of box b sits at b * 4 KiB + r * 128 + (c ^ (r % 8)) * 16, so the warp's
+// row-per-thread reads are conflict-free). The next group's load is issued as soon as the current
+// group has read its tile, so it overlaps the group's math and the next accumulator wait.
+struct LoadStage {
+  static constexpr int kTileBytes = 32 * 64 * 4;
+  static constexpr int kBytes = 8 * kTileBytes + 8 * 8 + 1024;  // tiles, one mbarrier per warp, alignment
+  uint8_t* tile;
+  uint64_t* bar;
+  uint32_t phase = 0;
+  bool pending = false;
+  __device__ void init(uint8_t* region, int ew, int lane) {
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(region) + 1023) & ~uintptr_t(1023));
+    tile = base + ew * kTileBytes;
+    bar = reinterpret_cast<uint64_t*>(base + 8 * kTileBytes) + ew;
+    if (lane == 0) {
+      mbar_init(bar, 1);
+      fence_mbarrier_init();
+    }
+    __syncwarp();
+  }
+  // warp-uniform: columns [col, col + 64) of rows [row0, row0 + 32)
+  __device__ void issue(const CUtensorMap* map, int col, int row0, int lane) {
+    fence_proxy_async_smem();  // this warp's reads of the tile come before the copy overwrites it
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar, kTileBytes);
+      tma_load_2d(tile, map, bar, col, row0);
+      tma_load_2d(tile + kTileBytes / 2, map, bar, col + 32, row0);
+    }
+    pending = true;
+  }
+  // bounded wait for the issued load; false (and the status word set) when it timed out
+  __device__ bool wait(int* status) {
+    pending = false;
+    const uint32_t par = phase;
+    phase ^= 1u;
+    if (mbar_try_wait(bar, par)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait_sleep(bar, par, 20000u)) {
+      if (clock64() - start > kWaitCycleBudget) {
+        if (status) atomicExch(status, kStatusWaitTimeout);
+        return false;
+      }
+    }
+    return true;
+  }
+  // floats 4 q .. 4 q + 3 of this thread's row (q = 0 .. 15)
+  __device__ float4 read4(int lane, int q) const {
+    return *reinterpret_cast<const float4*>(tile + (q >> 3) * (kTileBytes / 2) + lane * 128 +
+                                            (((q & 7) ^ (lane & 7)) << 4));
+  }
+};
+
 // Sum the kStatParts parts of a stats_a row into out[0..15].
 __device__ __forceinline__ void load_stats_a(const float* stats, int64_t row, float (&out)[16]) {
   const float* s = stats + (size_t)row * kStatParts * kStatStride;
@@ -219,6 +274,8 @@ struct EpiQkv {
 // ---------------------------------------------------------------------------------------------
 struct EpiProj {
   struct Params {
+    CUtensorMap tm_x;        // x [rows, 512] fp32, boxes of {32, 32}
+    int* status;
     PopCtx ctx;
     float* x;                // [rows, 512] fp32 residual stream, updated in place
     __nv_bfloat16* xb;       // [rows, 512] bf16 copy for the FC GEMM
@@ -226,7 +283,7 @@ struct EpiProj {
     float* stats_out;        // stats_b
     int layer;
   };
-  static constexpr int kSmemBytes = WarpVecs<2>::kBytes;
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes + LoadStage::kBytes;
   static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // [0] a_proj, [1] b_fc
@@ -235,11 +292,18 @@ struct EpiProj {
   float c2, ssq, dfc;
   SiteJitter jit;  // direct mode: draw added to the c_proj output (site 'attn')
   uint32_t patw[4];
+  LoadStage xs;     // the residual rows
+  int m_next = -1;  // this CTA's next 128-row tile
 
   __device__ EpiProj(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {}
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {
+    xs.init(smem + WarpVecs<2>::kBytes, ew, lane);
+  }
+
+  __device__ void next_unit(int m, int) { m_next = m; }
 
   __device__ void begin_mtile(int, int row) {
+    if (!xs.pending) xs.issue(&p.tm_x, half * 128, row - lane, lane);  // the first group of the first unit
     ri = row_info(p.ctx, row);
     float ys[8];
     ld_global_v8f(p.ystats + (size_t)row * kHeads, ys);
@@ -267,14 +331,22 @@ struct EpiProj {
         v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
     }
     float* xr = p.x + (size_t)row * kWidth + col;
+    xs.wait(p.status);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const float4 x4 = xs.read4(lane, q);
+      v[4 * q] += x4.x + c2 * a[4 * q];
+      v[4 * q + 1] += x4.y + c2 * a[4 * q + 1];
+      v[4 * q + 2] += x4.z + c2 * a[4 * q + 2];
+      v[4 * q + 3] += x4.w + c2 * a[4 * q + 3];
+    }
+    // the next group of this warp: the other 64 columns of its half, the next N tile, or the next unit
     {
-      float x8[8][8];  // all loads of the row segment in flight together
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ld_global_v8f(xr + 8 * j, x8[j]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[8 * j + u] += x8[j][u] + c2 * a[8 * j + u];
+      const int g = (col >> 6) & 1, n = col >> 8;
+      const int row0 = row - lane;
+      if (g == 0) xs.issue(&p.tm_x, col + 64, row0, lane);
+      else if (n + 1 < kWidth / 256) xs.issue(&p.tm_x, (n + 1) * 256 + half * 128, row0, lane);
+      else if (m_next >= 0) xs.issue(&p.tm_x, half * 128, m_next * 128 + (row0 & 127), lane);
     }
 #pragma unroll
     for (int j = 0; j < 64; j += 8) st_global_v8f(xr + j, v + j);
@@ -289,6 +361,11 @@ struct EpiProj {
 
   __device__ void end_mtile(int, int, int row) {
     *reinterpret_cast<float2*>(p.stats_out + ((size_t)row * 2 + half) * 2) = make_float2(ssq, dfc);
+  }
+
+  // a load issued for a group that never ran (a timed-out pipeline) lands before the CTA exits
+  __device__ void finish() {
+    if (xs.pending) xs.wait(p.status);
   }
 };
 

@@ -25,6 +25,8 @@
 //   __device__ void end_mtile(int m_tile, int n_tile, int row)     once per unit (n_tile = last one)
 // Optional:
 //   __device__ void finish()                                       once, after the last unit
+//   __device__ void next_unit(int m_tile, int n_begin)             at the start of each unit: the 128-row
+//                  tile and first N tile of this CTA's next unit (m_tile = -1: none), for prefetches
 #pragma once
 
 #include <type_traits>
@@ -57,6 +59,11 @@ struct TileUnit {
   }
   __host__ __device__ static int count(const GemmShape& s) { return kInterleaveN ? s.m_tiles * s.n_tiles : s.m_tiles; }
 };
+
+template <class E, class = void>
+struct HasNextUnit : std::false_type {};
+template <class E>
+struct HasNextUnit<E, std::void_t<decltype(&E::next_unit)>> : std::true_type {};
 
 template <class E, class = void>
 struct HasFinish : std::false_type {};
@@ -205,6 +212,15 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       const TileUnit<Epi::kInterleaveN> tu(u, shape);
       const int m = tu.m;
       const int row = m * L::BM + quarter * 32 + lane;
+      if constexpr (HasNextUnit<Epi>::value) {
+        const int un = u + (int)gridDim.x;
+        if (un < units) {
+          const TileUnit<Epi::kInterleaveN> tn(un, shape);
+          epi.next_unit(tn.m, tn.n_begin);
+        } else {
+          epi.next_unit(-1, 0);
+        }
+      }
       epi.begin_mtile(m, row);
       for (int n = tu.n_begin; n < tu.n_end; ++n, ++t) {
         const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;

@@ -170,6 +170,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Layout<kStages,
       const TileUnit<Epi::kInterleaveN> tu(u, shape);
       const int m = 2 * tu.m + (int)rank;  // this CTA's 128-row tile
       const int row = m * L::BM + quarter * 32 + lane;
+      if constexpr (HasNextUnit<Epi>::value) {
+        const int un = u + clusters;
+        if (un < units) {
+          const TileUnit<Epi::kInterleaveN> tn(un, shape);
+          epi.next_unit(2 * tn.m + (int)rank, tn.n_begin);
+        } else {
+          epi.next_unit(-1, 0);
+        }
+      }
       epi.begin_mtile(m, row);
       for (int n = tu.n_begin; n < tu.n_end; ++n, ++t) {
         const uint32_t acc = t % kAccs, acc_phase = (t / kAccs) & 1;

@@ -338,7 +338,9 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
       return rc;
     if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
     if (cap && !copy(cap->y + (size_t)l * rows * kWidth, w.y, rows * kWidth * 2)) return kStatusLaunchFailed;
-    EpiProj::Params pp{ctx, w.x, w.xb, w.ystats, w.st_b, l};
+    EpiProj::Params pp{{}, status, ctx, w.x, w.xb, w.ystats, w.st_b, l};
+    if (make_tmap_2d(&pp.tm_x, w.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, kWidth, kWidth, 32, 32))
+      return kStatusBadArgument;
     if ((rc = launch_gemm<EpiProj, kGemmStages>(w.y, wl + kPackProj, (int)rows, kWidth, kWidth, kWidth, kWidth, pp,
                                                    status, stream, kKindProj)))
       return rc;
