@@ -456,20 +456,23 @@ struct EpiFc {
 // after the last block, the head's input and stats. N-interleaved schedule: the two CTAs of an
 // M tile run together so the 512 KiB hidden tile is read from DRAM once.
 // ---------------------------------------------------------------------------------------------
-struct EpiMlpOut {
-  struct Params {
-    PopCtx ctx;
-    float* x;               // [rows, 512] residual stream, in place
-    __nv_bfloat16* xb;      // [rows, 512] next GEMM's operand
-    const float* hstats;    // [rows][2]
-    float* stats_out;       // stats_a
-    const float* wte;       // [4096, 512] fp32 token embedding (x0 recomputation)
-    const float* inv0;      // [rows] 1/rms of the perturbed embedding row
-    const float* lambdas;   // resid_lambdas[8] | x0_lambdas[8]
-    const float* wgate_next;  // [8, 32] fp32 of the next block, or nullptr
-    float* x_final;         // [rows, 512] fp32 output of the last block (capture only), or nullptr
-    int layer;
-  };
+struct MlpOutParams {
+  PopCtx ctx;
+  float* x;               // [rows, 512] residual stream, in place
+  __nv_bfloat16* xb;      // [rows, 512] next GEMM's operand
+  const float* hstats;    // [rows][2]
+  float* stats_out;       // stats_a
+  const float* wte;       // [4096, 512] fp32 token embedding (x0 recomputation)
+  const float* inv0;      // [rows] 1/rms of the perturbed embedding row
+  const float* lambdas;   // resid_lambdas[8] | x0_lambdas[8]
+  const float* wgate_next;  // [8, 32] fp32 of the next block, or nullptr
+  float* x_final;         // [rows, 512] fp32 output of the last block (capture only), or nullptr
+  int layer;
+};
+
+template <bool kDirect>
+struct EpiMlpOutT {
+  using Params = MlpOutParams;
   static constexpr int kSmemBytes = WarpVecs<6>::kBytes;
   static constexpr bool kInterleaveN = true;
   static constexpr bool kPair = true;  // K = 2048: the 2-SM engine halves the weight traffic per MMA
@@ -482,7 +485,7 @@ struct EpiMlpOut {
   SiteJitter jit, jit_wte;  // direct mode: site 'mlp' in this block; the embedding draw inside x0
   uint32_t patw[4], patw_wte[4];
 
-  __device__ EpiMlpOut(const Params& p_, uint8_t* smem, int ew, int lane_)
+  __device__ EpiMlpOutT(const Params& p_, uint8_t* smem, int ew, int lane_)
       : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 6 * 128), lane(lane_), half(ew >> 2),
         last(p_.layer == kLayers - 1) {}
 
@@ -500,8 +503,10 @@ struct EpiMlpOut {
       sa_wte = ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction);
       i0 = p.inv0[row];
     }
-    jit = site_jitter(p.ctx, p.layer, kSiteMlp, row, kWidth);
-    jit_wte = site_jitter(p.ctx, -1, kSiteWte, row, kWidth);  // on for every block when rerun from the embedding
+    if constexpr (kDirect) {
+      jit = site_jitter(p.ctx, p.layer, kSiteMlp, row, kWidth);
+      jit_wte = site_jitter(p.ctx, -1, kSiteWte, row, kWidth);  // on for every block when rerun from the embedding
+    }
   }
 
   __device__ void begin_tile(int m_tile, int, int col0) {
@@ -521,16 +526,20 @@ struct EpiMlpOut {
       warp_gauss128(vec + 256, p.ctx.key, kTidHead, 1, dir, col0, lane);
     }
     __syncwarp();
-    if (jit.on) site_patterns(p.ctx, kSiteMlp, jit.r, col0, patw);
-    if (jit_wte.on) site_patterns(p.ctx, kSiteWte, jit_wte.r, col0, patw_wte);
+    if constexpr (kDirect) {
+      if (jit.on) site_patterns(p.ctx, kSiteMlp, jit.r, col0, patw);
+      if (jit_wte.on) site_patterns(p.ctx, kSiteWte, jit_wte.r, col0, patw_wte);
+    }
   }
 
   __device__ void group(int row, int col, float (&v)[64]) {
     const int c = col & 127;
     const float* a = vec + c;
-    if (jit.on) {
+    if constexpr (kDirect) {
+      if (jit.on) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
+        for (int j = 0; j < 64; ++j) v[j] += jit.scale * draw_value(jit.r, col + j, patw[((col + j) & 127) >> 5]);
+      }
     }
     float* xr = p.x + (size_t)row * kWidth + col;
 #pragma unroll
@@ -560,7 +569,8 @@ struct EpiMlpOut {
           for (int u = 0; u < 8; ++u) {
             const int k = h + 8 * j + u;
             float ek = e8[j][u] + sa_wte * bw[k];
-            if (jit_wte.on) ek += jit_wte.scale * draw_value(jit_wte.r, col + k, patw_wte[((col + k) & 127) >> 5]);
+            if constexpr (kDirect)
+              if (jit_wte.on) ek += jit_wte.scale * draw_value(jit_wte.r, col + k, patw_wte[((col + k) & 127) >> 5]);
             const float x0 = ek * i0;
             v[k] = lr * v[k] + l0 * x0;
           }
@@ -611,6 +621,12 @@ struct EpiMlpOut {
 };
 
 // ---------------------------------------------------------------------------------------------
+
+// the population forward (rank-1 members) and the direct-draw reruns (site jitter) instantiate it apart,
+// so the former carries none of the jitter state
+using EpiMlpOut = EpiMlpOutT<false>;
+using EpiMlpOutDirect = EpiMlpOutT<true>;
+
 // Head: soft-capped logits of the whole vocabulary, reduced on the fly to the row's cross-entropy
 // pieces. |z| <= 15 after the soft cap, so sum exp(z - 15) needs no running maximum.
 // ---------------------------------------------------------------------------------------------

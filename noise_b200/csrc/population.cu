@@ -355,9 +355,11 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
     EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next,
                          (cap && l == kLayers - 1) ? cap->final_x : nullptr, l};
-    if ((rc = launch_gemm<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
-                                                     kHidden, mp, status, stream, kKindMlp)))
-      return rc;
+    rc = direct ? launch_gemm<EpiMlpOutDirect, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden,
+                                                            kHidden, kHidden, mp, status, stream, kKindMlp)
+                : launch_gemm<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
+                                                      kHidden, mp, status, stream, kKindMlp);
+    if (rc) return rc;
     if (cap && l + 1 < kLayers && !copy(cap->blocks + (size_t)(l + 1) * rows * kWidth, w.x, rows * kWidth * 4))
       return kStatusLaunchFailed;
   }
