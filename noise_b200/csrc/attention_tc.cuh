@@ -65,7 +65,8 @@ struct AttnTcLayout {
   static constexpr uint32_t kTmemCols = kGroupCols * G;
 };
 
-template <int G, int KT, bool kScore>
+// kDirect (population mode only): the DUST reruns' instantiation, which adds the 'o'-site draw.
+template <int G, int KT, bool kScore, bool kDirect = false>
 __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT == 64 ? 3 : 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnTcParams p) {
@@ -326,17 +327,25 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
       float o[64];
       tmem_ld64(tO + lane_addr, o);
       const float inv = 1.0f / ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
-      // direct mode: the draw added to the attention output (site 'o', before c_proj)
-      const SiteJitter jit = site_jitter(p.ctx, p.layer, kSiteO, row_base + q, kWidth);
-      uint32_t patw[4] = {0u, 0u, 0u, 0u};
-      if (jit.on) site_patterns(p.ctx, kSiteO, jit.r, (head * kHeadDim) & ~127, patw);
       float d = 0.f;
+      if constexpr (kDirect) {
+        // direct mode: the draw added to the attention output (site 'o', before c_proj)
+        const SiteJitter jit = site_jitter(p.ctx, p.layer, kSiteO, row_base + q, kWidth);
+        uint32_t patw[4] = {0u, 0u, 0u, 0u};
+        if (jit.on) site_patterns(p.ctx, kSiteO, jit.r, (head * kHeadDim) & ~127, patw);
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const int col = head * kHeadDim + j;
-        const float jv = jit.on ? jit.scale * draw_value(jit.r, col, patw[(col & 127) >> 5]) : 0.f;
-        o[j] = bf16_round(o[j] * inv + jv);
-        d += o[j] * bproj[j];
+        for (int j = 0; j < 64; ++j) {
+          const int col = head * kHeadDim + j;
+          const float jv = jit.on ? jit.scale * draw_value(jit.r, col, patw[(col & 127) >> 5]) : 0.f;
+          o[j] = bf16_round(o[j] * inv + jv);
+          d += o[j] * bproj[j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          o[j] = bf16_round(o[j] * inv);
+          d += o[j] * bproj[j];
+        }
       }
       st_bf16x64(p.y + (row_base + q) * kWidth + head * kHeadDim, o);
       p.ystats[(row_base + q) * kHeads + head] = d;

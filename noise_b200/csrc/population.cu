@@ -258,19 +258,19 @@ constexpr int kGemmStages = 3;  // 3 beats 4: the smaller carve-out leaves L1 to
 // 128-key tiles, half the hand-offs per key (parity-tested, measured slower: 923 ms)
 constexpr int kAttnKeyTile = 64;
 
-template <int G, int KT>
+template <int G, int KT, bool kDirect>
 int launch_attention_g(const CUtensorMap& tm, const AttnTcParams& ap, int64_t rows, cudaStream_t stream) {
   using L = AttnTcLayout<G, KT>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attention_tc_kernel<G, KT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
+    if (cudaFuncSetAttribute(attention_tc_kernel<G, KT, false, kDirect>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
         cudaSuccess)
       return kStatusLaunchFailed;
     configured = true;
   }
   dim3 grid(ap.ctx.T / (kAtQ * G), kHeads, (unsigned)(rows / ap.ctx.T));
   LaunchScope scope(kKindAttention, stream);
-  attention_tc_kernel<G, KT, false><<<grid, L::kThreads, L::kSmem, stream>>>(tm, tm, tm, ap);
+  attention_tc_kernel<G, KT, false, kDirect><<<grid, L::kThreads, L::kSmem, stream>>>(tm, tm, tm, ap);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
 
@@ -284,9 +284,14 @@ int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& 
   ap.status = status;
   ap.col_q = 0, ap.col_k = kWidth, ap.col_v = 2 * kWidth;
   const int n_qt = ctx.T / kAtQ;  // query tiles per sequence; a CTA takes 2 or 1 of them
-  if (kAttnKeyTile == 128) return launch_attention_g<1, 128>(tm, ap, rows, stream);
-  if (n_qt % 2 == 0) return launch_attention_g<2, 64>(tm, ap, rows, stream);
-  return launch_attention_g<1, 64>(tm, ap, rows, stream);
+  if (ctx.dir.on) {
+    if (kAttnKeyTile == 128) return launch_attention_g<1, 128, true>(tm, ap, rows, stream);
+    if (n_qt % 2 == 0) return launch_attention_g<2, 64, true>(tm, ap, rows, stream);
+    return launch_attention_g<1, 64, true>(tm, ap, rows, stream);
+  }
+  if (kAttnKeyTile == 128) return launch_attention_g<1, 128, false>(tm, ap, rows, stream);
+  if (n_qt % 2 == 0) return launch_attention_g<2, 64, false>(tm, ap, rows, stream);
+  return launch_attention_g<1, 64, false>(tm, ap, rows, stream);
 }
 
 // Optional copies of the clean forward's intermediates (one member, sigma = 0): what DUST's
