@@ -39,21 +39,21 @@ struct WarpVecs {
 // by its thread (16-byte chunk c of row r at position c ^ (r % 8): conflict-free), then lane 0 stores
 // the box with cp.async.bulk.tensor; a tile is rewritten only after the store issued from it two
 // groups earlier has read it.
-struct StoreStage {
+template <int kTiles>
+struct StoreStageT {
   static constexpr int kTileBytes = 32 * 128;
-  static constexpr int kBytes = 8 * 2 * kTileBytes + 1024;  // 8 warps x 2 tiles, plus alignment slack
-  uint8_t* tile[2];
+  static constexpr int kBytes = 8 * kTiles * kTileBytes + 1024;  // 8 warps x kTiles tiles, plus alignment slack
+  uint8_t* tile[kTiles];
   int next = 0;
   __device__ void init(uint8_t* region, int ew) {
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(region) + 1023) & ~uintptr_t(1023));
-    tile[0] = base + ew * 2 * kTileBytes;
-    tile[1] = tile[0] + kTileBytes;
+    for (int i = 0; i < kTiles; ++i) tile[i] = base + (ew * kTiles + i) * kTileBytes;
   }
   // v[0..63] of row (row0 + lane) -> global columns [col, col + 64) through the map
   __device__ void store64(const CUtensorMap* map, const float (&v)[64], int lane, int col, int row0) {
     uint8_t* t = tile[next];
-    next ^= 1;
-    if (lane == 0) tma_store_wait_read<1>();
+    next = (next + 1) % kTiles;
+    if (lane == 0) tma_store_wait_read<kTiles - 1>();
     __syncwarp();
     uint8_t* r = t + lane * 128;
 #pragma unroll
@@ -75,8 +75,8 @@ struct StoreStage {
   // the same with the 64 values already packed to bf16 pairs
   __device__ void store64_packed(const CUtensorMap* map, const uint32_t (&w)[32], int lane, int col, int row0) {
     uint8_t* t = tile[next];
-    next ^= 1;
-    if (lane == 0) tma_store_wait_read<1>();
+    next = (next + 1) % kTiles;
+    if (lane == 0) tma_store_wait_read<kTiles - 1>();
     __syncwarp();
     uint8_t* r = t + lane * 128;
 #pragma unroll
@@ -95,6 +95,8 @@ struct StoreStage {
     __syncwarp();
   }
 };
+
+using StoreStage = StoreStageT<2>;
 
 // Input staging for the fp32 residual rows an epilogue reads: each epilogue warp owns one 8 KiB tile
 // of 32 rows x 64 floats, filled by two {32 fp32, 32 rows} tensor-map boxes (128-byte swizzle: the
@@ -151,6 +153,57 @@ struct LoadStage {
   }
 };
 
+// The rotary table rows (bf16 cos[0..31] | sin[0..31], one 128-byte swizzled row per position) of a
+// warp's 32 consecutive positions, loaded once per M tile by one tensor-map box and read by every q
+// and k head of those rows.
+struct RopeStage {
+  static constexpr int kTileBytes = 32 * 128;
+  static constexpr int kBytes = 8 * kTileBytes + 8 * 8 + 1024;
+  uint8_t* tile;
+  uint64_t* bar;
+  uint32_t phase = 0;
+  bool pending = false;
+  __device__ void init(uint8_t* region, int ew, int lane) {
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(region) + 1023) & ~uintptr_t(1023));
+    tile = base + ew * kTileBytes;
+    bar = reinterpret_cast<uint64_t*>(base + 8 * kTileBytes) + ew;
+    if (lane == 0) {
+      mbar_init(bar, 1);
+      fence_mbarrier_init();
+    }
+    __syncwarp();
+  }
+  __device__ void issue(const CUtensorMap* map, int t0, int lane) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar, kTileBytes);
+      tma_load_2d(tile, map, bar, 0, t0);
+    }
+    pending = true;
+  }
+  __device__ void wait(int* status) {
+    pending = false;
+    const uint32_t par = phase;
+    phase ^= 1u;
+    if (mbar_try_wait(bar, par)) return;
+    const long long start = clock64();
+    while (!mbar_try_wait_sleep(bar, par, 20000u)) {
+      if (clock64() - start > kWaitCycleBudget) {
+        if (status) atomicExch(status, kStatusWaitTimeout);
+        return;
+      }
+    }
+  }
+  // cos (half 0) or sin (half 1) of frequencies 8 c .. 8 c + 7 (c = 0 .. 3) for this thread's position
+  __device__ void read8(int lane, int half, int c, float (&out)[8]) const {
+    const uint4 u = *reinterpret_cast<const uint4*>(tile + lane * 128 + (((4 * half + c) ^ (lane & 7)) << 4));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[2 * i] = __uint_as_float(w[i] << 16), out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+};
+
 // Sum the kStatParts parts of a stats_a row into out[0..15].
 __device__ __forceinline__ void load_stats_a(const float* stats, int64_t row, float (&out)[16]) {
   const float* s = stats + (size_t)row * kStatParts * kStatStride;
@@ -172,28 +225,36 @@ __device__ __forceinline__ void load_stats_a(const float* stats, int64_t row, fl
 struct EpiQkv {
   struct Params {
     CUtensorMap tm_qkv;     // qkv [rows, 1536] bf16, boxes of {64, 32}
+    CUtensorMap tm_rope;    // [T, 64] bf16 cos | sin, boxes of {64, 32}
+    int* status;
     PopCtx ctx;
     __nv_bfloat16* qkv;     // [rows, 1536]
     const float* stats;     // stats_a
-    const float* rope;      // [T][64]: cos[0..31] | sin[0..31]
     const float* ve_table;  // [4096, 512] or nullptr
     int layer;
   };
-  static constexpr int kSmemBytes = WarpVecs<2>::kBytes + StoreStage::kBytes;
+  // one store tile per warp: with the rotary rows staged too, a second would not fit beside 3 operand stages
+  static constexpr int kSmemBytes = WarpVecs<2>::kBytes + StoreStageT<1>::kBytes + RopeStage::kBytes;
   static constexpr bool kInterleaveN = false;
   const Params& p;
   float* vec;  // this warp's slots: [0] a of the tile's tensor, [1] b_ve
-  int lane;
+  int lane, half;
   RowInfo ri;
   float inv, xb[3], gate[kHeads], a_ve_tok;
-  StoreStage out;
+  StoreStageT<1> out;
+  RopeStage rs;
+  int m_next = -1;  // this CTA's next 128-row tile
 
   __device__ EpiQkv(const Params& p_, uint8_t* smem, int ew, int lane_)
-      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_) {
+      : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 2 * 128), lane(lane_), half(ew >> 2) {
     out.init(smem + WarpVecs<2>::kBytes, ew);
+    rs.init(smem + WarpVecs<2>::kBytes + StoreStageT<1>::kBytes, ew, lane);
   }
 
+  __device__ void next_unit(int m, int) { m_next = m; }
+
   __device__ void begin_mtile(int, int row) {
+    if (!rs.pending) rs.issue(&p.tm_rope, (row - lane) % p.ctx.T, lane);  // the first unit's rows
     ri = row_info(p.ctx, row);
     float st[16];
     load_stats_a(p.stats, row, st);
@@ -231,13 +292,13 @@ struct EpiQkv {
 #pragma unroll
     for (int j = 0; j < 64; ++j) v[j] = inv * (v[j] + c2 * a[j]);
     if (which < 2) {
-      const float* cs = p.rope + (size_t)ri.t * 64;
+      if (rs.pending) rs.wait(p.status);  // the M tile's first q or k group
       float ss = 0.f;
 #pragma unroll
       for (int j0 = 0; j0 < 32; j0 += 8) {
         float c[8], s[8];
-        ld_global_nc_v8f(cs + j0, c);
-        ld_global_nc_v8f(cs + 32 + j0, s);
+        rs.read8(lane, 0, j0 >> 3, c);
+        rs.read8(lane, 1, j0 >> 3, s);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int j = j0 + u;
@@ -250,6 +311,9 @@ struct EpiQkv {
       const float r = rms_scale(ss, kHeadDim);
 #pragma unroll
       for (int j = 0; j < 64; ++j) v[j] *= r;
+      // after this warp's last k group of the M tile the rows are free: fetch the next unit's
+      if (which == 1 && local == 256 + half * 128 + 64 && m_next >= 0)
+        rs.issue(&p.tm_rope, (m_next * 128 + ((row - lane) & 127)) % p.ctx.T, lane);
     } else if (has_ve(p.layer)) {
       const float* ve = p.ve_table + (size_t)ri.tok * kWidth + local;
       const float* bve = vec + 128 + (local & 127);
@@ -266,7 +330,10 @@ struct EpiQkv {
   }
 
   __device__ void end_mtile(int, int, int) {}
-  __device__ void finish() { out.drain(lane); }
+  __device__ void finish() {
+    if (rs.pending) rs.wait(p.status);  // a load issued for a unit that never ran lands before exit
+    out.drain(lane);
+  }
 };
 
 // ---------------------------------------------------------------------------------------------

@@ -227,6 +227,7 @@ struct PopWorkspace {
   float* hstats;
   float* inv0;
   float* part;
+  __nv_bfloat16* rope_bf16;  // [T][64] cos | sin as bf16 (the QKV epilogue's staged rotary rows)
 };
 
 // bytes per row of each buffer, in carve order
@@ -234,8 +235,11 @@ static const size_t kRowBytes[] = {
     kWidth * 4, kWidth * 2, 3 * kWidth * 2, kWidth * 2, kHidden * 2, kStatParts * kStatStride * 4, 2 * 2 * 4,
     kHeads * 4, 2 * 4, 4, 4 * 4};
 
+constexpr int kMaxT = 20480;
+constexpr size_t kRopeBf16Bytes = (size_t)kMaxT * kHeadDim * 2;
+
 size_t pop_workspace_bytes(int64_t rows) {
-  size_t total = 0;
+  size_t total = kRopeBf16Bytes;
   for (size_t b : kRowBytes) total += ((b * rows + 255) / 256) * 256;
   return total;
 }
@@ -249,7 +253,7 @@ PopWorkspace carve(void* ws, int64_t rows) {
   }
   return PopWorkspace{(float*)out[0], (__nv_bfloat16*)out[1], (__nv_bfloat16*)out[2], (__nv_bfloat16*)out[3],
                       (__nv_bfloat16*)out[4], (float*)out[5], (float*)out[6], (float*)out[7], (float*)out[8],
-                      (float*)out[9], (float*)out[10]};
+                      (float*)out[9], (float*)out[10], (__nv_bfloat16*)p};
 }
 
 constexpr int kGemmStages = 3;  // 3 beats 4: the smaller carve-out leaves L1 to the epilogues' table loads
@@ -307,6 +311,12 @@ struct CaptureBufs {
   float* logits;           // [rows][4096] raw logits before the soft cap
 };
 
+// The rotary table's bf16 copy (its values are bf16 already: exact).
+__global__ void rope_bf16_kernel(const float* __restrict__ rope, __nv_bfloat16* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __float2bfloat16_rn(rope[i]);
+}
+
 int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const float* rope, const PopCtx& ctx,
                       int members, float* losses, PopWorkspace& w, int* status, cudaStream_t stream,
                       const CaptureBufs* cap = nullptr) {
@@ -320,6 +330,14 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, stream) == cudaSuccess;
   };
   int rc;
+  {
+    const int n = ctx.T * kHeadDim;
+    LaunchScope scope(kKindOther, stream);
+    rope_bf16_kernel<<<(n + 255) / 256, 256, 0, stream>>>(rope, w.rope_bf16, n);
+  }
+  CUtensorMap tm_rope;
+  if (make_tmap_2d(&tm_rope, w.rope_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ctx.T, kHeadDim, kHeadDim, 32, 64))
+    return kStatusBadArgument;
   {
     EmbedParams ep{ctx, wte, lambdas, w.x, w.xb, w.inv0, w.st_a, cap ? cap->x0 : nullptr};
     if (first > 0 || (direct && ctx.dir.entry == 0)) {
@@ -335,7 +353,7 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
   }
   for (int l = first; l < kLayers; ++l) {
     const __nv_bfloat16* wl = packed + l * kPackLayer;
-    EpiQkv::Params q{{}, ctx, w.qkv, w.st_a, rope, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
+    EpiQkv::Params q{{}, tm_rope, status, ctx, w.qkv, w.st_a, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
     if (make_tmap_2d(&q.tm_qkv, w.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, 32, 64))
       return kStatusBadArgument;
     if ((rc = launch_gemm<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
@@ -384,7 +402,7 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
 }
 
 int check_pop_shape(int B, int T, int members) {
-  if (B <= 0 || T <= 0 || T % kAtQ || ((int64_t)B * T) % 128 || members <= 0 || T > 20480) return kStatusBadArgument;
+  if (B <= 0 || T <= 0 || T % kAtQ || ((int64_t)B * T) % 128 || members <= 0 || T > kMaxT) return kStatusBadArgument;
   return kStatusOk;
 }
 
