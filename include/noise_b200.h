@@ -72,6 +72,9 @@ typedef struct NoiseDirect {
   const float* x_entry; /* [B*T, 512] clean input of block `entry` (entry >= 0) */
   const float* inv0;    /* [B*T] clean 1/rms of the embedding rows (entry >= 0) */
   const void* live;     /* bf16 [B*T, 2048] clean relu^2 hidden of block `entry` (fc site) */
+  const void* y_entry;  /* optional bf16 [B*T, 512] clean attention output of block `entry` (entry >= 0):
+                           when given, block `entry` starts from it (plus the 'o' draw) instead of
+                           recomputing its QKV projection and attention, which no site changes */
 } NoiseDirect;
 
 /* Replaces DUST.rerun (train/val/run.py:256-279) for draws [draw_begin, draw_begin + draws) of the

@@ -72,7 +72,8 @@ class NoiseError(RuntimeError):
 class NoiseDirect(ctypes.Structure):
     """struct NoiseDirect of include/noise_b200.h."""
     _fields_ = [('entry', ctypes.c_int), ('mask', ctypes.c_uint32), ('site', ctypes.c_uint32 * 5),
-                ('sigma', ctypes.c_float), ('x_entry', c_void_p), ('inv0', c_void_p), ('live', c_void_p)]
+                ('sigma', ctypes.c_float), ('x_entry', c_void_p), ('inv0', c_void_p), ('live', c_void_p),
+                ('y_entry', c_void_p)]
 
 
 class NoisePrior(ctypes.Structure):

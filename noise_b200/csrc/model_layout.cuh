@@ -97,6 +97,7 @@ struct DirectSpec {
   const float* x_entry;           // [B*T, 512] clean input of block `entry` (entry >= 0)
   const float* inv0;              // [B*T] clean 1/rms of the embedding rows (entry >= 0)
   const __nv_bfloat16* live;      // [B*T, 2048] clean relu^2 hidden of block `entry`: > 0 marks live units
+  const __nv_bfloat16* y_entry;   // [B*T, 512] clean attention output of block `entry`, or nullptr
   float* token_loss;              // [members, B, T] per-token cross-entropy
 };
 

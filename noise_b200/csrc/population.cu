@@ -311,6 +311,36 @@ struct CaptureBufs {
   float* logits;           // [rows][4096] raw logits before the soft cap
 };
 
+// Direct reruns from block `entry`: every draw's attention output of that block is the clean one
+// (no site changes its q, k or v), plus the draw at site 'o' when that site is jittered; the rank-1
+// statistics of the (unperturbed) projection are zero. Eight columns per thread.
+__global__ void __launch_bounds__(256) direct_y_kernel(const __grid_constant__ PopCtx ctx, int layer,
+                                                       __nv_bfloat16* __restrict__ y, float* __restrict__ ystats,
+                                                       int64_t rows) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * (kWidth / 8)) return;
+  const int64_t row = i / (kWidth / 8);
+  const int c0 = (int)(i % (kWidth / 8)) * 8;
+  const int64_t e = row % ((int64_t)ctx.B * ctx.T);
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(ctx.dir.y_entry + e * kWidth + c0));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float v[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[2 * k] = __uint_as_float(w[k] << 16), v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+  const SiteJitter jit = site_jitter(ctx, layer, kSiteO, row, kWidth);
+  if (jit.on) {
+    const uint32_t pat = pattern_word(ctx.key, ctx.dir.site[kSiteO], jit.r.cycle, (uint32_t)c0 >> 5);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] += jit.scale * draw_value(jit.r, c0 + k, pat);
+  }
+  uint4 o;
+  o.x = pack_bf16x2(v[0], v[1]), o.y = pack_bf16x2(v[2], v[3]), o.z = pack_bf16x2(v[4], v[5]), o.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(y + row * kWidth + c0) = o;
+  if (c0 == 0)  // one thread per row clears the row's per-head statistics
+#pragma unroll
+    for (int k = 0; k < kHeads; ++k) ystats[row * kHeads + k] = 0.f;
+}
+
 // The rotary table's bf16 copy (its values are bf16 already: exact).
 __global__ void rope_bf16_kernel(const float* __restrict__ rope, __nv_bfloat16* __restrict__ out, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -356,10 +386,16 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     EpiQkv::Params q{{}, tm_rope, status, ctx, w.qkv, w.st_a, has_ve(l) ? params + L.offset[tid_ve(l)] : nullptr, l};
     if (make_tmap_2d(&q.tm_qkv, w.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 3 * kWidth, 3 * kWidth, 32, 64))
       return kStatusBadArgument;
-    if ((rc = launch_gemm<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
-                                                  q, status, stream, kKindQkv)))
-      return rc;
-    if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
+    if (direct && l == ctx.dir.entry && ctx.dir.y_entry) {
+      LaunchScope scope(kKindAttention, stream);
+      direct_y_kernel<<<(unsigned)((rows * (kWidth / 8) + 255) / 256), 256, 0, stream>>>(ctx, l, w.y, w.ystats, rows);
+      if (cudaGetLastError() != cudaSuccess) return kStatusLaunchFailed;
+    } else {
+      if ((rc = launch_gemm<EpiQkv, kGemmStages>(w.xb, wl + kPackQkv, (int)rows, 3 * kWidth, kWidth, kWidth, kWidth,
+                                                    q, status, stream, kKindQkv)))
+        return rc;
+      if ((rc = launch_attention(ctx, w.qkv, w, rows, l, status, stream))) return rc;
+    }
     if (cap && !copy(cap->y + (size_t)l * rows * kWidth, w.y, rows * kWidth * 2)) return kStatusLaunchFailed;
     EpiProj::Params pp{{}, status, ctx, w.x, w.xb, w.ystats, w.st_b, l};
     if (make_tmap_2d(&pp.tm_x, w.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, kWidth, kWidth, 32, 32))
@@ -481,6 +517,7 @@ extern "C" int noise_pop_forward_direct(const float* params, const void* packed,
     d.x_entry = spec->x_entry;
     d.inv0 = spec->inv0;
     d.live = reinterpret_cast<const __nv_bfloat16*>(spec->live);
+    d.y_entry = spec->entry >= 0 ? reinterpret_cast<const __nv_bfloat16*>(spec->y_entry) : nullptr;
     d.token_loss = token_loss + m0 * rows_per_member;
     PopCtx ctx{tokens, targets, T, B, draw_begin + m0, 1, 0.0f, PhiloxKey{seed, step}, d};
     PopWorkspace w = carve(workspace, rows_per_member * mc);

@@ -112,6 +112,7 @@ def rerun(w: Weights, cap: Capture, sites: list[Site], draws: int, draw_begin: i
         spec.x_entry = cap.blocks[entry].data_ptr()
         spec.inv0 = cap.inv0.data_ptr()
         spec.live = cap.hidden[entry].data_ptr()
+        spec.y_entry = cap.attn_out[entry].data_ptr()  # the entry block starts from its clean attention output
     out = torch.empty(draws, cap.B, cap.T, dtype=torch.float32, device=dev)
     per = max(1, min(draws, max_workspace // max(1, workspace_bytes(rows))))
     ws = workspace(dev, workspace_bytes(rows * per))
