@@ -288,7 +288,8 @@ int launch_attention(const PopCtx& ctx, const __nv_bfloat16* qkv, PopWorkspace& 
   ap.status = status;
   ap.col_q = 0, ap.col_k = kWidth, ap.col_v = 2 * kWidth;
   const int n_qt = ctx.T / kAtQ;  // query tiles per sequence; a CTA takes 2 or 1 of them
-  if (ctx.dir.on) {
+  // only block `entry` of a direct rerun adds a draw here (site 'o')
+  if (ctx.dir.on && layer == ctx.dir.entry && ((ctx.dir.mask >> kSiteO) & 1u)) {
     if (kAttnKeyTile == 128) return launch_attention_g<1, 128, true>(tm, ap, rows, stream);
     if (n_qt % 2 == 0) return launch_attention_g<2, 64, true>(tm, ap, rows, stream);
     return launch_attention_g<1, 64, true>(tm, ap, rows, stream);
@@ -414,7 +415,10 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
     EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next,
                          (cap && l == kLayers - 1) ? cap->final_x : nullptr, l};
-    rc = direct ? launch_gemm<EpiMlpOutDirect, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden,
+    // the direct instantiation where this block adds a draw: site 'mlp' of block `entry`, or the
+    // embedding draw inside x0 in every block of a rerun from the embedding
+    const bool jitter_here = direct && (l == ctx.dir.entry || ctx.dir.entry < 0);
+    rc = jitter_here ? launch_gemm<EpiMlpOutDirect, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden,
                                                             kHidden, kHidden, mp, status, stream, kKindMlp)
                 : launch_gemm<EpiMlpOut, kGemmStages>(w.hidden, wl + kPackMlp, (int)rows, kWidth, kHidden, kHidden,
                                                       kHidden, mp, status, stream, kKindMlp);
