@@ -5,8 +5,9 @@
 // One CTA = G consecutive 128-query tiles x one head x one (member, sequence) row block. The G tiles
 // share every K/V tile the CTA streams. The kernel is bound by the hand-offs between its roles, not
 // by the tensor or exp2 units, so it is sized for several independent CTAs per SM: G = 2, 96
-// registers, a 2-stage K/V ring (2 CTAs and 20 warps per SM; G = 1 when the tile count is odd). Warps:
-//   warp 0       TMA producer: the G Q tiles once, then 64-key K and V tiles into a 3-stage ring
+// registers, a 3-stage K ring and a 2-stage V ring (2 CTAs and 20 warps per SM; G = 1 when the tile
+// count is odd). Warps:
+//   warp 0       TMA producer: the G Q tiles once, then 64-key K and V tiles, K two tiles ahead of V
 //   warp 1       TMEM owner and MMA issuer (one thread), per key tile j and query tile g:
 //                  S_g  = Q_g K_j^T    tcgen05.mma M=128 N=64 K=64, A and B K-major
 //                  O_g += P_g V_j      tcgen05.mma M=128 N=64 K=64, A = P_g (K-major smem), B = V (MN-major)
@@ -46,17 +47,20 @@ struct AttnTcParams {
   int seqs;
 };
 
-constexpr int kAtQ = 128, kAtStages = 2;
+constexpr int kAtQ = 128;
 constexpr int kAtQBytes = kAtQ * kHeadDim * 2;  // 16 KB
 
 // G query tiles per CTA, key tiles of KT keys (64 or 128). A K or V tile is KT rows x 128 B; P is KT / 64
 // swizzled sub-tiles of 128 rows x 64 keys per query tile. TMEM per query tile: S (KT columns), then O.
+// K and V have rings of their own: a K stage is free once the S products have read it, a V stage
+// once the PV products have, and the producer keeps K kKStages - 1 tiles ahead of V.
 template <int G, int KT>
 struct AttnTcLayout {
   static constexpr int kThreads = (2 + 4 * G) * 32;
   static constexpr int kTileBytes = KT * kHeadDim * 2;
   static constexpr int kPBytes = kAtQ * KT * 2;
-  static constexpr int kCore = G * kAtQBytes + 2 * kAtStages * kTileBytes + G * kPBytes;
+  static constexpr int kKStages = KT == 64 ? 3 : 2, kVStages = 2;
+  static constexpr int kCore = G * kAtQBytes + (kKStages + kVStages) * kTileBytes + G * kPBytes;
   // 128-key tiles fit two CTAs per SM only without the alignment slack: the kernel then checks that
   // the dynamic shared base is 1024-aligned (it follows the per-CTA reserved kilobyte)
   static constexpr int kSlack = KT == 64 ? 1024 : 0;
@@ -76,14 +80,17 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const bool misaligned = L::kSlack == 0 && base != smem_raw;
   uint8_t* sQ = base;                              // [g] 16 KB
-  uint8_t* sK = sQ + G * kAtQBytes;                // [stage] KT x 128 B
-  uint8_t* sV = sK + kAtStages * kAtTileBytes;     // [stage] KT x 128 B
-  uint8_t* sP = sV + kAtStages * kAtTileBytes;     // [g] KT / 64 sub-tiles of 16 KB
+  constexpr int KS = L::kKStages, VS = L::kVStages;
+  uint8_t* sK = sQ + G * kAtQBytes;         // [stage] KT x 128 B
+  uint8_t* sV = sK + KS * kAtTileBytes;     // [stage] KT x 128 B
+  uint8_t* sP = sV + VS * kAtTileBytes;     // [g] KT / 64 sub-tiles of 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kCore);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = q_full + 1;            // [kAtStages]
-  uint64_t* kv_empty = kv_full + kAtStages;  // [kAtStages]
-  uint64_t* s_full = kv_empty + kAtStages;   // [G]
+  uint64_t* k_full = q_full + 1;      // [KS]
+  uint64_t* k_empty = k_full + KS;    // [KS]
+  uint64_t* v_full = k_empty + KS;    // [VS]
+  uint64_t* v_empty = v_full + VS;    // [VS]
+  uint64_t* s_full = v_empty + VS;    // [G]
   uint64_t* s_empty = s_full + G;            // [G]
   uint64_t* p_full = s_empty + G;            // [G]
   uint64_t* p_empty = p_full + G;            // [G]
@@ -112,7 +119,8 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kAtStages; ++s) mbar_init(&kv_full[s], 1), mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < KS; ++s) mbar_init(&k_full[s], 1), mbar_init(&k_empty[s], 1);
+    for (int s = 0; s < VS; ++s) mbar_init(&v_full[s], 1), mbar_init(&v_empty[s], 1);
     for (int g = 0; g < G; ++g) {
       mbar_init(&s_full[g], 1);
       mbar_init(&s_empty[g], 4);
@@ -153,22 +161,29 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
         for (int b = 0; b < 2 * G; ++b)
           tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_q, q_full, qcol, (int)(rq + q0 + 64 * b));
       }
-      int issued = 0;
-      for (int j = 0; j < n_kt; ++j) {
-        const int st = j % kAtStages;
-        if (!mbar_wait(&kv_empty[st], ((j / kAtStages) & 1) ^ 1, abort_flag, status)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kAtTileBytes);
+      // order K(0) .. K(KS - 2), then K(j + KS - 1) before V(j): each wait is for a stage that the
+      // products issued before the one the next copy feeds have released
+      int nk = 0, nv = 0;
+      bool ok = true;
+      auto load = [&](bool key, int j) {
+        const int stages = key ? KS : VS, st = j % stages;
+        uint64_t* full = key ? &k_full[st] : &v_full[st];
+        if (!mbar_wait(key ? &k_empty[st] : &v_empty[st], ((j / stages) & 1) ^ 1, abort_flag, status)) return false;
+        mbar_arrive_expect_tx(full, kAtTileBytes);
+        uint8_t* dst = (key ? sK : sV) + st * kAtTileBytes;
         const int r = (kt_begin + j) * kAtK;
-        for (int h = 0; h < KT / 64; ++h) {  // boxes of 64 rows
-          tma_load_2d(sK + st * kAtTileBytes + h * 8192, &tm_k, &kv_full[st], kcol, (int)(rk + r + 64 * h));
-          tma_load_2d(sV + st * kAtTileBytes + h * 8192, &tm_v, &kv_full[st], vcol, (int)(rv + r + 64 * h));
-        }
-        issued = j + 1;
+        for (int h = 0; h < KT / 64; ++h)  // boxes of 64 rows
+          tma_load_2d(dst + h * 8192, key ? &tm_k : &tm_v, full, key ? kcol : vcol, (int)((key ? rk : rv) + r + 64 * h));
+        return true;
+      };
+      while (ok && nv < n_kt) {
+        if (nk < n_kt && nk < nv + KS - 1) ok = load(true, nk++);
+        else ok = load(false, nv++);
       }
       // copies in flight land before the CTA can exit
       if (!misaligned) mbar_wait(q_full, 0, abort_flag, status);
-      for (int j = max(0, issued - kAtStages); j < issued; ++j)
-        mbar_wait(&kv_full[j % kAtStages], (j / kAtStages) & 1, abort_flag, status);
+      for (int j = max(0, nk - KS); j < nk; ++j) mbar_wait(&k_full[j % KS], (j / KS) & 1, abort_flag, status);
+      for (int j = max(0, nv - VS); j < nv; ++j) mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -179,8 +194,8 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
       tc_fence_after();
       for (int j = 0; ok && j <= n_kt; ++j) {
         if (j < n_kt) {
-          const int st = j % kAtStages;
-          if (!mbar_wait(&kv_full[st], (j / kAtStages) & 1, abort_flag, status)) {
+          const int st = j % KS;
+          if (!mbar_wait(&k_full[st], (j / KS) & 1, abort_flag, status)) {
             ok = false;
             break;
           }
@@ -199,9 +214,15 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
               tc_mma_f16(tmem + L::kGroupCols * g, dq + 2 * k, dk + 2 * k, idesc_s, k > 0 ? 1u : 0u);
             tc_commit(&s_full[g]);
           }
+          if (ok) tc_commit(&k_empty[st]);
         }
         if (ok && j > 0) {
-          const int jj = j - 1, st = jj % kAtStages;
+          const int jj = j - 1, st = jj % VS;
+          if (!mbar_wait(&v_full[st], (jj / VS) & 1, abort_flag, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const uint64_t dv = smem_desc_sw128_mn(sV + st * kAtTileBytes);
           for (int g = 0; g < G && ok; ++g) {
             const int lo = g_lo(g);
@@ -219,7 +240,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
             }
             tc_commit(&p_empty[g]);
           }
-          if (ok) tc_commit(&kv_empty[st]);
+          if (ok) tc_commit(&v_empty[st]);
         }
       }
       if (ok) tc_commit(o_full);
@@ -238,7 +259,9 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
     const uint32_t tS = tmem + L::kGroupCols * g, tO = tS + KT;
     const float kScaleLog2 = 0.125f * 1.4426950408889634f;
     const float kOffsetLog2 = 8.0f * 1.4426950408889634f;
-    float lsum[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+    // packed fp32 pairs (sm_100 f32x2 FMA / add): two independent partial row sums of two lanes each
+    const float2 kScale2 = make_float2(kScaleLog2, kScaleLog2), kNegOffset2 = make_float2(-kOffsetLog2, -kOffsetLog2);
+    float2 lsum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     bool ok = true;
     uint8_t* prow = sP + g * kAtPBytes + r * 128;
     const int qlo = qg + quarter * 32, qhi = qlo + 31;  // this warp's rows
@@ -268,29 +291,47 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int kc = k0 + 64 * h + 32 * c;
-        // warp-uniform classification of the 32 x 32 block (this warp's rows x the chunk's keys)
+        // warp-uniform classification of the 32 x 32 block (this warp's rows x the chunk's keys):
+        // fully visible blocks take a path without per-key masks
         const bool none = kc > qhi || qlo - (kc + 31) > p.window;
         const bool all = (kc + 31 <= qlo) && (qhi - kc <= p.window);
+        // P row r: 16-byte chunk (4c + b) of 8 keys stored at (4c + b) ^ (r % 8) (128-byte swizzle)
+        auto store = [&](int b, const uint32_t (&w)[4]) {
+          *reinterpret_cast<uint4*>(ph + (((4 * c + b) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        };
+        if (all) {
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {  // 8 keys = one 16-byte chunk of the P row
-          uint32_t w[4] = {0u, 0u, 0u, 0u};
-          if (!none) {
+          for (int b = 0; b < 4; ++b) {
+            uint32_t w[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int i = 32 * c + 8 * b + 2 * u;
-              float e0 = ex2_approx(sv[i] * kScaleLog2 - kOffsetLog2);
-              float e1 = ex2_approx(sv[i + 1] * kScaleLog2 - kOffsetLog2);
-              if (!all) {
-                const int key = kc + 8 * b + 2 * u;
-                if (key > q || q - key > p.window) e0 = 0.f;
-                if (key + 1 > q || q - key - 1 > p.window) e1 = 0.f;
-              }
-              lsum[u] += e0 + e1;
-              w[u] = pack_bf16x2(e0, e1);
+              const float2 x = __ffma2_rn(make_float2(sv[i], sv[i + 1]), kScale2, kNegOffset2);
+              const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              lsum[u & 1] = __fadd2_rn(lsum[u & 1], e);
+              w[u] = pack_bf16x2(e.x, e.y);
             }
+            store(b, w);
           }
-          // P row r: chunk (4c + b) stored at (4c + b) ^ (r % 8) (128-byte swizzle)
-          *reinterpret_cast<uint4*>(ph + (((4 * c + b) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            if (!none) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int i = 32 * c + 8 * b + 2 * u;
+                const float2 x = __ffma2_rn(make_float2(sv[i], sv[i + 1]), kScale2, kNegOffset2);
+                float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                const int key = kc + 8 * b + 2 * u;
+                if (key > q || q - key > p.window) e.x = 0.f;
+                if (key + 1 > q || q - key - 1 > p.window) e.y = 0.f;
+                lsum[u & 1] = __fadd2_rn(lsum[u & 1], e);
+                w[u] = pack_bf16x2(e.x, e.y);
+              }
+            }
+            store(b, w);
+          }
         }
       }
       }
@@ -304,7 +345,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
         tc_fence_after();
         float o[64];
         tmem_ld64(tO + lane_addr, o);
-        const float inv = 1.0f / ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
+        const float inv = 1.0f / ((lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y));
         const int64_t trow = (int64_t)((int)blockIdx.z % p.seqs) * T + q;
         const uint4* tg = reinterpret_cast<const uint4*>(p.target + trow * kWidth + head * kHeadDim);
         float d = 0.f;
@@ -326,7 +367,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
       tc_fence_after();
       float o[64];
       tmem_ld64(tO + lane_addr, o);
-      const float inv = 1.0f / ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3]));
+      const float inv = 1.0f / ((lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y));
       float d = 0.f;
       if constexpr (kDirect) {
         // direct mode: the draw added to the attention output (site 'o', before c_proj)
