@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
   if (!kScore && tid >= 64 && tid < 80) {  // the member's c_proj column factor for this head's 64 columns
     const RowInfo r0 = row_info(p.ctx, row_base);
     reinterpret_cast<float4*>(bproj)[tid - 64] =
-        gauss4(p.ctx.key, (head * kHeadDim >> 2) + (tid - 64), tid_proj(p.layer), 1, r0.direction);
+        draw4(p.ctx, r0.slot, tid_proj(p.layer), 1, (head * kHeadDim >> 2) + (tid - 64));
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, L::kTmemCols);

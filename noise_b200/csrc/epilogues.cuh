@@ -262,15 +262,15 @@ struct EpiQkv {
 #pragma unroll
     for (int i = 0; i < 3; ++i) xb[i] = st[1 + i];
     if (has_ve(p.layer)) {
-      const float4 ag0 = gauss4(p.ctx.key, 0, tid_gate(p.layer), 0, ri.direction);
-      const float4 ag1 = gauss4(p.ctx.key, 1, tid_gate(p.layer), 0, ri.direction);
+      const float4 ag0 = draw4(p.ctx, ri.slot, tid_gate(p.layer), 0, 0);
+      const float4 ag1 = draw4(p.ctx, ri.slot, tid_gate(p.layer), 0, 1);
       const float ag[8] = {ag0.x, ag0.y, ag0.z, ag0.w, ag1.x, ag1.y, ag1.z, ag1.w};
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) {
         const float pre = inv * (st[5 + h] + ri.sign * st[4] * ag[h]);
         gate[h] = 2.0f / (1.0f + expf(-pre));
       }
-      a_ve_tok = gauss1(p.ctx.key, ri.tok, tid_ve(p.layer), 0, ri.direction);
+      a_ve_tok = draw1(p.ctx, ri.slot, tid_ve(p.layer), 0, ri.tok);
     }
   }
 
@@ -280,8 +280,8 @@ struct EpiQkv {
     const int which = col0 / kWidth, local = col0 % kWidth;
     const uint32_t tid = which == 0 ? tid_q(p.layer) : which == 1 ? tid_k(p.layer) : tid_v(p.layer);
     __syncwarp();
-    warp_gauss128(vec, p.ctx.key, tid, 0, r0.direction, local, lane);
-    if (which == 2 && has_ve(p.layer)) warp_gauss128(vec + 128, p.ctx.key, tid_ve(p.layer), 1, r0.direction, local, lane);
+    warp_draw128(vec, p.ctx, r0.slot, tid, 0, local, lane);
+    if (which == 2 && has_ve(p.layer)) warp_draw128(vec + 128, p.ctx, r0.slot, tid_ve(p.layer), 1, local, lane);
     __syncwarp();
   }
 
@@ -383,8 +383,8 @@ struct EpiProj {
   __device__ void begin_tile(int m_tile, int, int col0) {
     const RowInfo r0 = row_info(p.ctx, (int64_t)m_tile * 128);
     __syncwarp();
-    warp_gauss128(vec, p.ctx.key, tid_proj(p.layer), 0, r0.direction, col0, lane);
-    warp_gauss128(vec + 128, p.ctx.key, tid_fc(p.layer), 1, r0.direction, col0, lane);
+    warp_draw128(vec, p.ctx, r0.slot, tid_proj(p.layer), 0, col0, lane);
+    warp_draw128(vec + 128, p.ctx, r0.slot, tid_fc(p.layer), 1, col0, lane);
     __syncwarp();
     if (jit.on) site_patterns(p.ctx, kSiteAttn, jit.r, col0, patw);
   }
@@ -476,8 +476,8 @@ struct EpiFc {
   __device__ void begin_tile(int m_tile, int, int col0) {
     const RowInfo r0 = row_info(p.ctx, (int64_t)m_tile * 128);
     __syncwarp();
-    warp_gauss128(vec, p.ctx.key, tid_fc(p.layer), 0, r0.direction, col0, lane);
-    warp_gauss128(vec + 128, p.ctx.key, tid_mlp(p.layer), 1, r0.direction, col0, lane);
+    warp_draw128(vec, p.ctx, r0.slot, tid_fc(p.layer), 0, col0, lane);
+    warp_draw128(vec + 128, p.ctx, r0.slot, tid_mlp(p.layer), 1, col0, lane);
     __syncwarp();
     if (jit.on) site_patterns(p.ctx, kSiteFc, jit.r, col0, patw);
   }
@@ -565,9 +565,9 @@ struct EpiMlpOutT {
     for (int h = 0; h < kHeads; ++h) gp[h] = 0.f;
     if (!last) {
       const int nl = p.layer + 1;
-      lr = p.lambdas[nl] + ri.sign * gauss1(p.ctx.key, nl, kTidResid, 0, ri.direction);
-      l0 = p.lambdas[kLayers + nl] + ri.sign * gauss1(p.ctx.key, nl, kTidX0, 0, ri.direction);
-      sa_wte = ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction);
+      lr = p.lambdas[nl] + ri.sign * draw1(p.ctx, ri.slot, kTidResid, 0, nl);
+      l0 = p.lambdas[kLayers + nl] + ri.sign * draw1(p.ctx, ri.slot, kTidX0, 0, nl);
+      sa_wte = ri.sign * draw1(p.ctx, ri.slot, kTidWte, 0, ri.tok);
       i0 = p.inv0[row];
     }
     if constexpr (kDirect) {
@@ -578,19 +578,19 @@ struct EpiMlpOutT {
 
   __device__ void begin_tile(int m_tile, int, int col0) {
     const RowInfo r0 = row_info(p.ctx, (int64_t)m_tile * 128);
-    const uint32_t dir = r0.direction;
+    const uint32_t slot = r0.slot;
     __syncwarp();
-    warp_gauss128(vec, p.ctx.key, tid_mlp(p.layer), 0, dir, col0, lane);
+    warp_draw128(vec, p.ctx, slot, tid_mlp(p.layer), 0, col0, lane);
     if (!last) {
       const int nl = p.layer + 1;
-      warp_gauss128(vec + 128, p.ctx.key, kTidWte, 1, dir, col0, lane);
-      warp_gauss128(vec + 256, p.ctx.key, tid_q(nl), 1, dir, col0, lane);
-      warp_gauss128(vec + 384, p.ctx.key, tid_k(nl), 1, dir, col0, lane);
-      warp_gauss128(vec + 512, p.ctx.key, tid_v(nl), 1, dir, col0, lane);
+      warp_draw128(vec + 128, p.ctx, slot, kTidWte, 1, col0, lane);
+      warp_draw128(vec + 256, p.ctx, slot, tid_q(nl), 1, col0, lane);
+      warp_draw128(vec + 384, p.ctx, slot, tid_k(nl), 1, col0, lane);
+      warp_draw128(vec + 512, p.ctx, slot, tid_v(nl), 1, col0, lane);
       if (has_ve(nl) && col0 == 0 && lane < 8)  // b_gate has 32 entries
-        reinterpret_cast<float4*>(vec + 640)[lane] = gauss4(p.ctx.key, lane, tid_gate(nl), 1, dir);
+        reinterpret_cast<float4*>(vec + 640)[lane] = draw4(p.ctx, slot, tid_gate(nl), 1, lane);
     } else {
-      warp_gauss128(vec + 256, p.ctx.key, kTidHead, 1, dir, col0, lane);
+      warp_draw128(vec + 256, p.ctx, slot, kTidHead, 1, col0, lane);
     }
     __syncwarp();
     if constexpr (kDirect) {
@@ -728,7 +728,7 @@ struct EpiHead {
   __device__ void begin_tile(int m_tile, int, int col0) {
     const RowInfo r0 = row_info(p.ctx, (int64_t)m_tile * 128);
     __syncwarp();
-    warp_gauss128(vec, p.ctx.key, kTidHead, 0, r0.direction, col0, lane);
+    warp_draw128(vec, p.ctx, r0.slot, kTidHead, 0, col0, lane);
     __syncwarp();
   }
 

@@ -112,7 +112,71 @@ struct PopCtx {
   float sigma;         // member j perturbs by +sigma (even j) or -sigma (odd j); 0 in direct mode
   PhiloxKey key;
   DirectSpec dir;
+  // The chunk's draw table (see DrawTable): slot s holds direction (dir_first + s) mod P.
+  const float* draws = nullptr;
+  int64_t dir_first = 0;
+  int slots = 0;
 };
+
+// ---------------------------------------------------------------------------------------------
+// Draw table. Every rank-1 draw vector a (vec 0, length out) and b (vec 1, length in) of every
+// tensor depends only on (key, tensor, vec, direction), yet the GEMM epilogues need the same
+// 128-column slices for every 128-row tile of a member. One kernel per chunk writes each direction's
+// vectors once (gauss4 of the same counters, so the values are identical) and the epilogues load
+// them: [slot][tensor][vec][len], lengths padded to 4 floats.
+// ---------------------------------------------------------------------------------------------
+__host__ __device__ constexpr int draw_len(int t, int v) {
+  if (t == (int)kTidResid || t == (int)kTidX0) return v ? 4 : kLayers;
+  if (t == (int)kTidWte || t == (int)kTidHead || t >= 56) return v ? kWidth : kVocab;
+  for (int l = 0; l < kLayers; ++l) {
+    const int k = t - (int)tid_base(l);
+    if (k < 0 || k > (has_ve(l) ? 6 : 5)) continue;
+    if (k < 4) return kWidth;                                       // c_q, c_k, c_v, c_proj
+    if (has_ve(l) && k == 4) return v ? kGateChannels : kHeads;     // ve_gate [8, 32]
+    const bool fc = k == (has_ve(l) ? 5 : 4);
+    return fc ? (v ? kWidth : kHidden) : (v ? kHidden : kWidth);   // c_fc [2048, 512], mlp.c_proj [512, 2048]
+  }
+  return 0;
+}
+
+struct DrawTable {
+  int32_t off[kNumTensors][2];
+  int32_t per_slot;
+};
+
+__host__ __device__ constexpr DrawTable make_draw_table() {
+  DrawTable d{};
+  int32_t o = 0;
+  for (int t = 0; t < kNumTensors; ++t)
+    for (int v = 0; v < 2; ++v) {
+      d.off[t][v] = o;
+      o += draw_len(t, v);
+    }
+  d.per_slot = o;
+  return d;
+}
+
+constexpr int kDrawPerSlot = make_draw_table().per_slot;  // floats per direction (101,548)
+constexpr int kDrawMaxSlots = 512;                        // directions one chunk may span
+static __constant__ DrawTable kDrawTableDev = make_draw_table();
+
+// Slots a chunk of `members` members starting at member_begin spans.
+__host__ __device__ inline int draw_slots(int64_t member_begin, int members, int pairs) {
+  const int span = (int)((members + (member_begin & 1) + 1) / 2);
+  return span < pairs ? span : pairs;
+}
+
+__device__ __forceinline__ const float* draw_ptr(const PopCtx& c, uint32_t slot, uint32_t tensor, uint32_t vec) {
+  return c.draws + (size_t)slot * kDrawPerSlot + kDrawTableDev.off[tensor][vec];
+}
+
+// element i of draw vector (tensor, vec) of a slot; four elements from 4 * blk
+__device__ __forceinline__ float draw1(const PopCtx& c, uint32_t slot, uint32_t tensor, uint32_t vec, uint32_t i) {
+  return __ldg(draw_ptr(c, slot, tensor, vec) + i);
+}
+__device__ __forceinline__ float4 draw4(const PopCtx& c, uint32_t slot, uint32_t tensor, uint32_t vec, uint32_t blk) {
+  return __ldg(reinterpret_cast<const float4*>(draw_ptr(c, slot, tensor, vec)) + blk);
+}
 
 // Jitter of a direct-mode site in one row: the draw's Hadamard row and sign, and scale.
 struct SiteJitter {
@@ -144,6 +208,7 @@ __device__ __forceinline__ void site_patterns(const PopCtx& c, uint32_t kind, co
 
 struct RowInfo {
   uint32_t direction;
+  uint32_t slot;  // the direction's slot in the chunk's draw table
   float sign;
   int t;    // position in the sequence
   int tok;  // input token id
@@ -156,6 +221,8 @@ __device__ __forceinline__ RowInfo row_info(const PopCtx& c, int64_t row) {
   const int64_t j = c.member_begin + row / seq_rows;
   const int64_t within = row % seq_rows;
   r.direction = (uint32_t)((j % (2 * (int64_t)c.pairs)) >> 1);
+  const int64_t s = (int64_t)r.direction - c.dir_first;
+  r.slot = (uint32_t)(s < 0 ? s + c.pairs : s);
   r.sign = (j & 1) ? -c.sigma : c.sigma;
   r.t = (int)(within % c.T);
   r.tok = __ldg(c.tokens + within);
@@ -163,12 +230,11 @@ __device__ __forceinline__ RowInfo row_info(const PopCtx& c, int64_t row) {
   return r;
 }
 
-// Fill dst[0..127] (per-warp shared memory) with elements e0 .. e0+127 of the stream
-// (tensor, vec, direction); e0 % 4 == 0. Caller brackets with __syncwarp().
-__device__ __forceinline__ void warp_gauss128(float* dst, PhiloxKey key, uint32_t tensor, uint32_t vec,
-                                              uint32_t direction, uint32_t e0, int lane) {
-  const float4 g = gauss4(key, (e0 >> 2) + lane, tensor, vec, direction);
-  reinterpret_cast<float4*>(dst)[lane] = g;
+// Fill dst[0..127] (per-warp shared memory) with elements e0 .. e0+127 of draw vector (tensor, vec)
+// of a slot of the draw table; e0 % 4 == 0. Caller brackets with __syncwarp().
+__device__ __forceinline__ void warp_draw128(float* dst, const PopCtx& c, uint32_t slot, uint32_t tensor, uint32_t vec,
+                                             uint32_t e0, int lane) {
+  reinterpret_cast<float4*>(dst)[lane] = draw4(c, slot, tensor, vec, (e0 >> 2) + lane);
 }
 
 }  // namespace noise

@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
   for (int i = tid; i < 4 * (kWidth / 4); i += blockDim.x) {
     const int v = i / (kWidth / 4), blk = i % (kWidth / 4);
     const uint32_t tensor = v == 0 ? kTidWte : v == 1 ? tid_q(0) : v == 2 ? tid_k(0) : tid_v(0);
-    sv[v][blk] = p.ctx.sigma != 0.f ? gauss4(p.ctx.key, blk, tensor, 1, r0.direction) : make_float4(0.f, 0.f, 0.f, 0.f);
+    sv[v][blk] = p.ctx.sigma != 0.f ? draw4(p.ctx, r0.slot, tensor, 1, blk) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const SiteJitter j0 = site_jitter(p.ctx, -1, kSiteWte, row0, kWidth);  // same draw for the whole CTA
   if (j0.on && tid < kWidth / 128) {
@@ -54,12 +54,12 @@ __global__ void __launch_bounds__(256) embed_kernel(const __grid_constant__ Embe
     for (int k = 0; k < 4; ++k) patw[tid * 4 + k] = w[k];
   }
   __syncthreads();
-  const float mix = p.lambdas[0] + r0.sign * gauss1(p.ctx.key, 0, kTidResid, 0, r0.direction) + p.lambdas[kLayers] +
-                    r0.sign * gauss1(p.ctx.key, 0, kTidX0, 0, r0.direction);
+  const float mix = p.lambdas[0] + r0.sign * draw1(p.ctx, r0.slot, kTidResid, 0, 0) + p.lambdas[kLayers] +
+                    r0.sign * draw1(p.ctx, r0.slot, kTidX0, 0, 0);
   for (int rr = warp; rr < kEmbedRows; rr += 8) {
     const int64_t row = row0 + rr;
     const RowInfo ri = row_info(p.ctx, row);
-    const float sa = p.ctx.sigma != 0.f ? ri.sign * gauss1(p.ctx.key, ri.tok, kTidWte, 0, ri.direction) : 0.f;
+    const float sa = p.ctx.sigma != 0.f ? ri.sign * draw1(p.ctx, ri.slot, kTidWte, 0, ri.tok) : 0.f;
     const SiteJitter jit = site_jitter(p.ctx, -1, kSiteWte, row, kWidth);
     const float4* w = reinterpret_cast<const float4*>(p.wte + (size_t)ri.tok * kWidth);
     float4 e[4];
@@ -228,6 +228,7 @@ struct PopWorkspace {
   float* inv0;
   float* part;
   __nv_bfloat16* rope_bf16;  // [T][64] cos | sin as bf16 (the QKV epilogue's staged rotary rows)
+  float* draws;              // [slots][kDrawPerSlot] the chunk's draw table
 };
 
 // bytes per row of each buffer, in carve order
@@ -238,8 +239,15 @@ static const size_t kRowBytes[] = {
 constexpr int kMaxT = 20480;
 constexpr size_t kRopeBf16Bytes = (size_t)kMaxT * kHeadDim * 2;
 
+// Draw-table slots a workspace for `rows` rows holds: a chunk of m members spans at most m / 2 + 1
+// directions and has at least 128 rows per member.
+int64_t draw_capacity(int64_t rows) {
+  const int64_t cap = rows / 256 + 2;
+  return cap < kDrawMaxSlots ? cap : kDrawMaxSlots;
+}
+
 size_t pop_workspace_bytes(int64_t rows) {
-  size_t total = kRopeBf16Bytes;
+  size_t total = kRopeBf16Bytes + ((draw_capacity(rows) * kDrawPerSlot * 4 + 255) / 256) * 256;
   for (size_t b : kRowBytes) total += ((b * rows + 255) / 256) * 256;
   return total;
 }
@@ -253,7 +261,26 @@ PopWorkspace carve(void* ws, int64_t rows) {
   }
   return PopWorkspace{(float*)out[0], (__nv_bfloat16*)out[1], (__nv_bfloat16*)out[2], (__nv_bfloat16*)out[3],
                       (__nv_bfloat16*)out[4], (float*)out[5], (float*)out[6], (float*)out[7], (float*)out[8],
-                      (float*)out[9], (float*)out[10], (__nv_bfloat16*)p};
+                      (float*)out[9], (float*)out[10], (__nv_bfloat16*)p, (float*)(p + kRopeBf16Bytes)};
+}
+
+// Point a chunk's context at its draw table (filled by draw_table_kernel at the start of the chunk).
+void attach_draws(PopCtx& c, const PopWorkspace& w, int members) {
+  c.draws = w.draws;
+  c.dir_first = (c.member_begin % (2 * (int64_t)c.pairs)) >> 1;
+  c.slots = draw_slots(c.member_begin, members, c.pairs);
+}
+
+// Block (x, tensor * 2 + vec, slot): float4 x of the vector, the same gauss4 the epilogues used to draw.
+__global__ void __launch_bounds__(256) draw_table_kernel(PhiloxKey key, int64_t dir_first, int pairs,
+                                                         float* __restrict__ table) {
+  const int t = blockIdx.y >> 1, v = blockIdx.y & 1;
+  const int blk = blockIdx.x * blockDim.x + threadIdx.x;
+  if (blk * 4 >= draw_len(t, v)) return;
+  const uint32_t slot = blockIdx.z;
+  const uint32_t direction = (uint32_t)((dir_first + slot) % pairs);
+  reinterpret_cast<float4*>(table + (size_t)slot * kDrawPerSlot + kDrawTableDev.off[t][v])[blk] =
+      gauss4(key, (uint32_t)blk, (uint32_t)t, (uint32_t)v, direction);
 }
 
 constexpr int kGemmStages = 3;  // 3 beats 4: the smaller carve-out leaves L1 to the epilogues' table loads
@@ -366,6 +393,13 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
     LaunchScope scope(kKindOther, stream);
     rope_bf16_kernel<<<(n + 255) / 256, 256, 0, stream>>>(rope, w.rope_bf16, n);
   }
+  if (ctx.draws != w.draws || ctx.slots <= 0 || ctx.slots > draw_capacity(rows)) return kStatusBadArgument;
+  {
+    LaunchScope scope(kKindOther, stream);
+    const dim3 grid((kVocab / 4 + 255) / 256, 2 * kNumTensors, (unsigned)ctx.slots);
+    draw_table_kernel<<<grid, 256, 0, stream>>>(ctx.key, ctx.dir_first, ctx.pairs, w.draws);
+    if (cudaGetLastError() != cudaSuccess) return kStatusLaunchFailed;
+  }
   CUtensorMap tm_rope;
   if (make_tmap_2d(&tm_rope, w.rope_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ctx.T, kHeadDim, kHeadDim, 32, 64))
     return kStatusBadArgument;
@@ -446,9 +480,11 @@ int check_pop_shape(int B, int T, int members) {
   return kStatusOk;
 }
 
-int pop_chunk_members(int64_t rows_per_member, int members, size_t workspace_bytes) {
+int pop_chunk_members(int64_t rows_per_member, int members, int pairs, size_t workspace_bytes) {
   int chunk = members;
   while (chunk > 0 && pop_workspace_bytes(rows_per_member * chunk) > workspace_bytes) --chunk;
+  // the chunk's directions fit the draw table (at most chunk / 2 + 1 of them, and at most P)
+  while (chunk > 0 && draw_slots(1, chunk, pairs) > draw_capacity(rows_per_member * chunk)) --chunk;
   while (chunk > 0 && (int64_t)chunk * rows_per_member > (int64_t)1 << 30) --chunk;  // int32 GEMM row indices
   return chunk;
 }
@@ -480,13 +516,14 @@ extern "C" int noise_pop_forward_lowrank(const float* params, const void* packed
   if (!params || !packed || !rope || !tokens || !targets || !losses || !workspace) return kStatusBadArgument;
   if (check_pop_shape(B, T, members) || pairs <= 0 || member_begin < 0) return kStatusBadArgument;
   const int64_t rows_per_member = (int64_t)B * T;
-  const int chunk = pop_chunk_members(rows_per_member, members, workspace_bytes);
+  const int chunk = pop_chunk_members(rows_per_member, members, pairs, workspace_bytes);
   if (chunk == 0) return kStatusWorkspaceTooSmall;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < members; m0 += chunk) {
     const int mc = members - m0 < chunk ? members - m0 : chunk;
     PopCtx ctx{tokens, targets, T, B, member_begin + m0, pairs, sigma, PhiloxKey{seed, step}, DirectSpec{}};
     PopWorkspace w = carve(workspace, rows_per_member * mc);
+    attach_draws(ctx, w, mc);
     const int rc = pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, mc,
                                      losses + m0, w, status, s);
     if (rc) return rc;
@@ -507,7 +544,7 @@ extern "C" int noise_pop_forward_direct(const float* params, const void* packed,
   if (spec->entry >= 0 && ((spec->mask & 1u) || !spec->x_entry || !spec->inv0)) return kStatusBadArgument;
   if (((spec->mask >> kSiteFc) & 1u) && !spec->live) return kStatusBadArgument;
   const int64_t rows_per_member = (int64_t)B * T;
-  const int chunk = pop_chunk_members(rows_per_member, draws, workspace_bytes);
+  const int chunk = pop_chunk_members(rows_per_member, draws, 1, workspace_bytes);
   if (chunk == 0) return kStatusWorkspaceTooSmall;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < draws; m0 += chunk) {
@@ -525,6 +562,7 @@ extern "C" int noise_pop_forward_direct(const float* params, const void* packed,
     d.token_loss = token_loss + m0 * rows_per_member;
     PopCtx ctx{tokens, targets, T, B, draw_begin + m0, 1, 0.0f, PhiloxKey{seed, step}, d};
     PopWorkspace w = carve(workspace, rows_per_member * mc);
+    attach_draws(ctx, w, mc);
     const int rc = pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, mc, nullptr,
                                      w, status, s);
     if (rc) return rc;
@@ -546,6 +584,7 @@ extern "C" int noise_pop_capture(const float* params, const void* packed, const 
                   reinterpret_cast<__nv_bfloat16*>(out->hidden), out->final_x, out->logits};
   PopCtx ctx{tokens, targets, T, B, 0, 1, 0.0f, PhiloxKey{0, 0}, DirectSpec{}};
   PopWorkspace w = carve(workspace, rows);
+  attach_draws(ctx, w, 1);
   return pop_forward_chunk(params, reinterpret_cast<const __nv_bfloat16*>(packed), rope, ctx, 1, out->token_loss, w,
                            status, reinterpret_cast<cudaStream_t>(stream), &cap);
 }
