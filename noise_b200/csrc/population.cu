@@ -486,7 +486,10 @@ int pop_chunk_members(int64_t rows_per_member, int members, int pairs, size_t wo
   // the chunk's directions fit the draw table (at most chunk / 2 + 1 of them, and at most P)
   while (chunk > 0 && draw_slots(1, chunk, pairs) > draw_capacity(rows_per_member * chunk)) --chunk;
   while (chunk > 0 && (int64_t)chunk * rows_per_member > (int64_t)1 << 30) --chunk;  // int32 GEMM row indices
-  return chunk;
+  if (chunk == 0) return 0;
+  // as many chunks as the largest fitting one needs, of equal size: no short tail chunk
+  const int n = (members + chunk - 1) / chunk;
+  return (members + n - 1) / n;
 }
 
 }  // namespace noise
