@@ -38,7 +38,7 @@ def oracle_losses(params, members, pairs, sigma, rows):
     (1, 128, 4, 2, 1e-3),
     (2, 256, 4, 2, 2e-3),
     (1, 1152, 2, 1, 1e-3),   # the 1024-token windows bind
-    (1, 128, 6, 4, 0.05),    # members beyond 2P wrap onto earlier directions; a large sigma
+    (1, 128, 6, 4, 0.05),    # a large sigma
 ])
 def test_population_matches_oracle(weights, params_cpu, B, T, members, pairs, sigma):
     from noise_b200.population import population_losses
@@ -59,6 +59,25 @@ def test_member_offset_and_chunking(weights):
     small = population_losses(weights, x, y, 0, 8, 4, 1e-3, SEED, STEP, max_workspace=workspace_bytes(3 * 128)).cpu()
     assert torch.equal(full, part)
     assert torch.equal(full, small)
+
+
+def test_chunks_wrap_and_odd_starts(weights, params_cpu):
+    """Members past 2P wrap onto earlier directions. Pieces that start on odd members, and a workspace
+    that forces three-member chunks, give the losses of one call bit for bit (each chunk's draw table
+    maps the directions it spans to its own slots). The one call matches the oracle."""
+    from noise_b200.population import population_losses, workspace_bytes
+    rows = zipf_tokens(1, 129, seed=7)
+    x, y = rows[:, :-1], rows[:, 1:]
+    members, pairs, sigma = 11, 3, 1e-2
+    full = population_losses(weights, x, y, 0, members, pairs, sigma, SEED, STEP).cpu()
+    part = torch.cat([population_losses(weights, x, y, m0, n, pairs, sigma, SEED, STEP).cpu()
+                      for m0, n in ((0, 3), (3, 5), (8, 3))])
+    small = population_losses(weights, x, y, 0, members, pairs, sigma, SEED, STEP,
+                              max_workspace=workspace_bytes(3 * 128)).cpu()
+    assert torch.equal(full, part)
+    assert torch.equal(full, small)
+    want = oracle_losses(params_cpu, np.arange(members), pairs, sigma, rows)
+    np.testing.assert_allclose(full.numpy(), want, rtol=1e-3)
 
 
 def test_deterministic(weights):
