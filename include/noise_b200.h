@@ -43,17 +43,20 @@ int64_t noise_packed_count(void);
  * that autocast performs in train/val/eggroll.py:144). */
 int noise_pack_weights(const float* params, void* packed, void* stream);
 
-/* Workspace bytes for `rows` population rows (rows = members * B * T of one chunk). */
+/* Workspace bytes for `rows` population rows (rows = members * B * T of one chunk): the per-row
+ * activations, the bf16 rotary table and the chunk's draw table (406 KB per direction the chunk
+ * spans, for at most min(512, rows / 256 + 2) directions). */
 size_t noise_pop_workspace_bytes(int64_t rows);
 
 /* Replaces train/val/eggroll.py:66-103 (population_loss, through Eggroll.loss at :115/:145) for
  * members [member_begin, member_begin + members): member j perturbs every parameter by
  * s_j * (a_d b_d^T) (rank-1 factors for matrices and embeddings, eps_d for the mixing scalars) with
  * d = (j mod 2*pairs) / 2 and s_j = +sigma for even j, -sigma for odd j (:134-146). Draw d is
- * regenerated from the Philox stream keyed by (seed, step). Every member evaluates all B rows of
+ * regenerated from the Philox stream keyed by (seed, step), once per chunk into the workspace's draw
+ * table. Every member evaluates all B rows of
  * tokens/targets ([B, T] int32, T % 128 == 0) and losses[j - member_begin] receives
  * its mean next-token cross-entropy over B*T tokens. rope: [T][64] fp32 = bf16-rounded cos | sin
- * (utils/model.py:177-183). Members are processed in chunks that fit `workspace`. */
+ * (utils/model.py:177-183). Members are processed in equal chunks that fit `workspace`. */
 int noise_pop_forward_lowrank(const float* params, const void* packed, const float* rope, const int32_t* tokens,
                               const int32_t* targets, int B, int T, int64_t member_begin, int members, int pairs,
                               float sigma, uint32_t seed, uint32_t step, float* losses, void* workspace,
