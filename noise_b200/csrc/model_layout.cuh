@@ -156,7 +156,7 @@ __host__ __device__ constexpr DrawTable make_draw_table() {
   return d;
 }
 
-constexpr int kDrawPerSlot = make_draw_table().per_slot;  // floats per direction (101,548)
+constexpr int kDrawPerSlot = make_draw_table().per_slot;  // floats per direction (101,560)
 constexpr int kDrawMaxSlots = 512;                        // directions one chunk may span
 static __constant__ DrawTable kDrawTableDev = make_draw_table();
 
