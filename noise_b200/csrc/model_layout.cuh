@@ -127,7 +127,7 @@ struct PopCtx {
 // ---------------------------------------------------------------------------------------------
 __host__ __device__ constexpr int draw_len(int t, int v) {
   if (t == (int)kTidResid || t == (int)kTidX0) return v ? 4 : kLayers;
-  if (t == (int)kTidWte || t == (int)kTidHead || t >= 56) return v ? kWidth : kVocab;
+  if (t == (int)kTidWte || t == (int)kTidHead || t >= (int)tid_ve(0)) return v ? kWidth : kVocab;  // by token
   for (int l = 0; l < kLayers; ++l) {
     const int k = t - (int)tid_base(l);
     if (k < 0 || k > (has_ve(l) ? 6 : 5)) continue;
@@ -156,7 +156,15 @@ __host__ __device__ constexpr DrawTable make_draw_table() {
   return d;
 }
 
-constexpr int kDrawPerSlot = make_draw_table().per_slot;  // floats per direction (101,560)
+__host__ __device__ constexpr bool draw_lengths_aligned() {
+  for (int t = 0; t < kNumTensors; ++t)
+    if (draw_len(t, 0) % 4 || draw_len(t, 1) % 4 || draw_len(t, 0) == 0) return false;
+  return true;
+}
+static_assert(draw_lengths_aligned(), "draw vectors are read as float4 and every tensor has one");
+
+constexpr int kDrawPerSlot = make_draw_table().per_slot;  // floats per direction
+static_assert(kDrawPerSlot == 101560, "the documented draw-table size (406,240 B per direction)");
 constexpr int kDrawMaxSlots = 512;                        // directions one chunk may span
 static __constant__ DrawTable kDrawTableDev = make_draw_table();
 
