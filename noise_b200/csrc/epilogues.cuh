@@ -6,7 +6,8 @@
 // where the row scale s is the RMS-norm of the layer input (applied here instead of on the operand:
 // norm(x) W^T = (x W^T) / rms(x)), s_m = +-sigma is the member's sign, and x . b_m is a per-row scalar
 // that the *producer* of x computed as a side statistic, so the GEMM itself is the plain shared-weight
-// product. a_m is regenerated from the counter-based stream into per-warp shared memory.
+// product. a_m's 128-column slice is copied into per-warp shared memory from the chunk's draw table
+// (the counter-based stream, written once per chunk by draw_table_kernel).
 //
 // Row statistics travel between kernels as partial sums (the consumer adds the parts):
 //   stats_a (QKV / head input x), float [rows][4][16]:
@@ -15,7 +16,8 @@
 //   stats_b (FC input x), float [rows][2][2]: sum x^2, x.b_fc
 //   hstats (MLP-out input), float [rows][2]: hidden.b_mlp
 // Dot products use the bf16 values the next GEMM reads; sums of squares use the fp32 stream.
-// Every row segment moves through 32-byte (full-sector) per-thread loads and stores.
+// Row segments move through 32-byte (full-sector) per-thread loads and stores, or through TMA where
+// an epilogue stages them (QKV and FC outputs, proj's residual rows, QKV's rotary rows).
 #pragma once
 
 #include "gemm_tc.cuh"

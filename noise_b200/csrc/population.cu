@@ -11,8 +11,10 @@
 //         MLP GEMM   x += hidden Wm^T (+rank-1); next block's mixed input + stats }
 //   head GEMM        soft-capped logits -> per-row log-sum-exp pieces
 //   member loss      mean over the member's B*T rows
-// No noise tensor is ever materialised: every kernel regenerates its draws from (seed, step,
-// direction, tensor).
+// No noise tensor is ever materialised: the draws are the counter-based stream of (seed, step,
+// direction, tensor). Each chunk starts with draw_table_kernel, which writes the rank-1 vectors of
+// the directions it spans (a few hundred KB each) for the epilogues, the embedding and the attention
+// to read; the direct-mode jitter is regenerated where it is added.
 #include "attention_tc.cuh"
 #include "epilogues.cuh"
 #include "gemm_tc2.cuh"
