@@ -1,5 +1,5 @@
 """Fitness shaping, Sigma f eps + AdamW and a whole Eggroll.step on the GPU, against the oracle and the
-reference's golden vectors. Tolerances: ranks bit-exact; update cosine >= 0.999 and
+reference's golden vectors. Tolerances: ranks bit-exact; update cosine >= 0.999 (the parity bar for the update) and
 elementwise rtol 1e-4 on the reconstructed gradient; AdamW deltas rtol 2e-3."""
 from pathlib import Path
 
