@@ -16,7 +16,7 @@ import torch
 
 from . import _lib
 from .model import LAYERS, TENSOR_ID, VOCAB, WIDTH, Weights
-from .population import workspace, workspace_bytes
+from .population import units_that_fit, workspace, workspace_bytes
 
 HIDDEN = 4 * WIDTH
 SITE_KINDS = {'transformer.wte': 0, 'o': 1, 'attn': 2, 'fc': 3, 'mlp': 4}
@@ -114,7 +114,7 @@ def rerun(w: Weights, cap: Capture, sites: list[Site], draws: int, draw_begin: i
         spec.live = cap.hidden[entry].data_ptr()
         spec.y_entry = cap.attn_out[entry].data_ptr()  # the entry block starts from its clean attention output
     out = torch.empty(draws, cap.B, cap.T, dtype=torch.float32, device=dev)
-    per = max(1, min(draws, max_workspace // max(1, workspace_bytes(rows))))
+    per = units_that_fit(rows, draws, max_workspace)
     ws = workspace(dev, workspace_bytes(rows * per))
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     _lib.call('noise_pop_forward_direct', w.flat.data_ptr(), w.packed.data_ptr(), w.rope(cap.T).data_ptr(),

@@ -31,6 +31,20 @@ def workspace_bytes(rows: int) -> int:
     return int(_lib.load().noise_pop_workspace_bytes(rows))
 
 
+def units_that_fit(rows_per_unit: int, units: int, max_workspace: int) -> int:
+    """The most units (members or draws) of rows_per_unit rows whose workspace fits max_workspace, at
+    least 1. The workspace has parts that do not grow with the rows (the rotary table, a capped draw
+    table), so this searches the size query instead of dividing by one unit's size."""
+    lo, hi = 1, max(1, units)
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if workspace_bytes(rows_per_unit * mid) <= max_workspace:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
 def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, member_begin: int, members: int,
                       pairs: int, sigma: float, seed: int, step: int, out: torch.Tensor | None = None,
                       status: torch.Tensor | None = None, max_workspace: int | None = None) -> torch.Tensor:
@@ -46,7 +60,7 @@ def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, m
     rows_per_member = B * T
     if max_workspace is None:
         max_workspace = DEFAULT_WORKSPACE_BYTES
-    per_chunk = max(1, min(members, max_workspace // max(1, workspace_bytes(rows_per_member))))
+    per_chunk = units_that_fit(rows_per_member, members, max_workspace)
     ws = workspace(dev, workspace_bytes(rows_per_member * per_chunk))
     own_status = status is None
     if own_status:

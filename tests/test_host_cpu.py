@@ -30,3 +30,15 @@ def test_recipe_splits_over_ranks(world):
         rec = recipe(scale)
         counts = rec.writers + rec.hidden + rec.hubs + [rec.embedding] + list(rec.local.values())
         assert all(k % world == 0 for k in counts) and 8 % world == 0
+
+
+def test_units_that_fit_uses_the_whole_workspace():
+    """The largest block of members (or draws) whose population workspace fits, found on the size
+    query (which has parts that do not grow with the rows), at least one."""
+    from noise_b200.population import units_that_fit, workspace_bytes
+    rows = 8 * 2048
+    for budget in (workspace_bytes(rows), 16 << 30, 32 << 30):
+        n = units_that_fit(rows, 4096, budget)
+        assert workspace_bytes(rows * n) <= budget < workspace_bytes(rows * (n + 1))
+    assert units_that_fit(rows, 5, 32 << 30) == 5
+    assert units_that_fit(rows, 100, 1) == 1
