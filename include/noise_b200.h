@@ -48,6 +48,15 @@ int noise_pack_weights(const float* params, void* packed, void* stream);
  * spans, for at most min(512, rows / 256 + 2) directions). */
 size_t noise_pop_workspace_bytes(int64_t rows);
 
+/* Members per chunk that noise_pop_forward_lowrank (pairs = P) or noise_pop_forward_direct (pairs = 1)
+ * processes for `members` members of rows_per_member rows each, given workspace_bytes: the largest
+ * chunk whose workspace fits, whose directions fit the draw table and whose rows fit 32-bit GEMM row
+ * indices, then evened out so that all chunks have the same size (0: not even one member fits).
+ * Sizing the workspace as noise_pop_workspace_bytes(rows_per_member * chunk) gives a buffer that the
+ * call uses in full. No reference counterpart (the reference's chunk is the fixed CHUNK = 256 pairs,
+ * train/val/eggroll.py:35). */
+int noise_pop_chunk_members(int64_t rows_per_member, int members, int pairs, size_t workspace_bytes);
+
 /* Replaces train/val/eggroll.py:66-103 (population_loss, through Eggroll.loss at :115/:145) for
  * members [member_begin, member_begin + members): member j perturbs every parameter by
  * s_j * (a_d b_d^T) (rank-1 factors for matrices and embeddings, eps_d for the mixing scalars) with

@@ -29,6 +29,7 @@ SIGNATURES: dict[str, tuple] = {
     'noise_packed_count': (c_int64, []),
     'noise_pack_weights': (c_int, [c_void_p, c_void_p, c_void_p]),
     'noise_pop_workspace_bytes': (c_size_t, [c_int64]),
+    'noise_pop_chunk_members': (c_int, [c_int64, c_int, c_int, c_size_t]),
     'noise_pop_forward_lowrank': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int64,
                                           c_int, c_int, c_float, c_uint32, c_uint32, c_void_p, c_void_p, c_size_t,
                                           c_void_p, c_void_p]),

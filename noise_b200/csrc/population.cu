@@ -500,6 +500,11 @@ using namespace noise;
 
 extern "C" size_t noise_pop_workspace_bytes(int64_t rows) { return pop_workspace_bytes(rows); }
 
+extern "C" int noise_pop_chunk_members(int64_t rows_per_member, int members, int pairs, size_t workspace_bytes) {
+  if (rows_per_member <= 0 || members <= 0 || pairs <= 0) return 0;
+  return pop_chunk_members(rows_per_member, members, pairs, workspace_bytes);
+}
+
 extern "C" int64_t noise_param_count(void) { return make_param_layout().total; }
 
 extern "C" int64_t noise_packed_count(void) { return kPackTotal; }

@@ -115,11 +115,12 @@ def rerun(w: Weights, cap: Capture, sites: list[Site], draws: int, draw_begin: i
         spec.y_entry = cap.attn_out[entry].data_ptr()  # the entry block starts from its clean attention output
     out = torch.empty(draws, cap.B, cap.T, dtype=torch.float32, device=dev)
     per = units_that_fit(rows, draws, max_workspace)
-    ws = workspace(dev, workspace_bytes(rows * per))
+    need = workspace_bytes(rows * per)
+    ws = workspace(dev, need)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     _lib.call('noise_pop_forward_direct', w.flat.data_ptr(), w.packed.data_ptr(), w.rope(cap.T).data_ptr(),
               cap.x.data_ptr(), cap.y.data_ptr(), cap.B, cap.T, draw_begin, draws, _lib.ctypes.byref(spec),
-              seed & 0xFFFFFFFF, step & 0xFFFFFFFF, out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
+              seed & 0xFFFFFFFF, step & 0xFFFFFFFF, out.data_ptr(), ws.data_ptr(), need, status.data_ptr(),
               _stream(dev))
     if int(status.item()):
         raise _lib.NoiseError('direct rerun: device wait timed out')

@@ -31,18 +31,13 @@ def workspace_bytes(rows: int) -> int:
     return int(_lib.load().noise_pop_workspace_bytes(rows))
 
 
-def units_that_fit(rows_per_unit: int, units: int, max_workspace: int) -> int:
-    """The most units (members or draws) of rows_per_unit rows whose workspace fits max_workspace, at
-    least 1. The workspace has parts that do not grow with the rows (the rotary table, a capped draw
-    table), so this searches the size query instead of dividing by one unit's size."""
-    lo, hi = 1, max(1, units)
-    while lo < hi:
-        mid = (lo + hi + 1) // 2
-        if workspace_bytes(rows_per_unit * mid) <= max_workspace:
-            lo = mid
-        else:
-            hi = mid - 1
-    return lo
+def units_that_fit(rows_per_unit: int, units: int, max_workspace: int, pairs: int = 1) -> int:
+    """Members (or draws) per chunk the library will use for `units` units of rows_per_unit rows under a
+    max_workspace budget: noise_pop_chunk_members, the library's own chunking (largest fitting chunk,
+    capped by the draw table and 32-bit row indices, then evened out), at least 1. pairs: the
+    population's antithetic directions (1 for direct draws)."""
+    n = int(_lib.load().noise_pop_chunk_members(rows_per_unit, max(1, units), max(1, pairs), max_workspace))
+    return max(1, n)
 
 
 def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, member_begin: int, members: int,
@@ -60,14 +55,15 @@ def population_losses(w: Weights, tokens: torch.Tensor, targets: torch.Tensor, m
     rows_per_member = B * T
     if max_workspace is None:
         max_workspace = DEFAULT_WORKSPACE_BYTES
-    per_chunk = units_that_fit(rows_per_member, members, max_workspace)
-    ws = workspace(dev, workspace_bytes(rows_per_member * per_chunk))
+    per_chunk = units_that_fit(rows_per_member, members, max_workspace, pairs)
+    need = workspace_bytes(rows_per_member * per_chunk)
+    ws = workspace(dev, need)
     own_status = status is None
     if own_status:
         status = torch.zeros(1, dtype=torch.int32, device=dev)
     _lib.call('noise_pop_forward_lowrank', w.flat.data_ptr(), w.packed.data_ptr(), w.rope(T).data_ptr(),
               tok.data_ptr(), tgt.data_ptr(), B, T, member_begin, members, pairs, float(sigma), seed & 0xFFFFFFFF,
-              step & 0xFFFFFFFF, out.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
+              step & 0xFFFFFFFF, out.data_ptr(), ws.data_ptr(), need, status.data_ptr(),
               torch.cuda.current_stream(dev).cuda_stream)
     if own_status:
         code = int(status.item())

@@ -32,13 +32,24 @@ def test_recipe_splits_over_ranks(world):
         assert all(k % world == 0 for k in counts) and 8 % world == 0
 
 
-def test_units_that_fit_uses_the_whole_workspace():
-    """The largest block of members (or draws) whose population workspace fits, found on the size
-    query (which has parts that do not grow with the rows), at least one."""
+def test_units_that_fit_is_the_library_chunking():
+    """The host sizes its workspace from the library's own chunk query: the chunk's workspace fits
+    the budget, the number of chunks is the fewest that any fitting chunk allows, the chunks are
+    equal, and the draw table's direction cap binds for rank-1 populations."""
     from noise_b200.population import units_that_fit, workspace_bytes
     rows = 8 * 2048
     for budget in (workspace_bytes(rows), 16 << 30, 32 << 30):
-        n = units_that_fit(rows, 4096, budget)
-        assert workspace_bytes(rows * n) <= budget < workspace_bytes(rows * (n + 1))
+        largest = 1
+        while workspace_bytes(rows * (largest + 1)) <= budget:
+            largest += 1
+        for units in (1, 7, 1024, 4096):
+            n = units_that_fit(rows, units, budget)
+            assert workspace_bytes(rows * n) <= budget
+            assert -(-units // n) == -(-units // min(units, largest)), (budget, units, n, largest)
+            assert n == -(-units // -(-units // n))  # chunks of equal size, no short tail
     assert units_that_fit(rows, 5, 32 << 30) == 5
     assert units_that_fit(rows, 100, 1) == 1
+    # rank-1 members: a chunk spans at most rows / 256 + 2 directions of the draw table
+    short = 128
+    n = units_that_fit(short, 4096, 32 << 30, pairs=2048)
+    assert (n + 1) // 2 <= short * n // 256 + 2

@@ -50,6 +50,21 @@ def test_static_scratch_matches_allocating_entry_point(mode):
         assert torch.equal(w, w_ref), f'call {call}: weights differ'
 
 
+def test_static_scratch_without_ranks_buffer():
+    """Mode 0 (the z-score fitness Eggroll uses by default) with no ranks buffer: the rank kernel is
+    skipped and the pair differences read only the losses; two calls in a row, bit-equal weights."""
+    from noise_b200 import _lib
+    rng = np.random.default_rng(7)
+    for call, (n, pairs) in enumerate([(4096, 2048), (1024, 256)]):
+        losses = torch.from_numpy((8.3 + 1e-3 * rng.standard_normal(n)).astype(np.float32)).cuda()
+        w_ref, _ = _allocating(losses, pairs, 0)
+        w = torch.empty(pairs, device='cuda')
+        _lib.call('noise_fitness_static', losses.data_ptr(), n, pairs, 0, w.data_ptr(), None,
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.equal(w, w_ref), f'call {call}: weights differ'
+
+
 def test_static_scratch_limit():
     from noise_b200 import _lib
     lib = _lib.load()
