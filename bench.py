@@ -7,7 +7,7 @@ per-member CE losses, NCCL all-gather of losses (N > 1), centred-rank fitness, S
 reconstruction fused with AdamW (lr 1e-3), packed-weight refresh.
 
     python bench.py [--gpus N --steps K --warmup W]          # this repository's CUDA path
-    python bench.py --impl reference [...]                   # the CPU restatement of the reference path
+    python bench.py --impl reference [...]                   # the reference's own ES update on the host cores
     python bench.py --workload dust [--dust-scale S]          # seconds per DUST update (a separate line)
 Multi-GPU: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
 Rank 0 prints one JSON line.
@@ -117,30 +117,67 @@ def dist_setup():
     return rank, world, local
 
 
-def reference_sample(members: int = 2, length: int = SEQ, steps: int = 1):
-    """Time the CPU restatement of the reference's population forward (oracle port) on the host."""
+def sdpa_window(q, k, v, window):
+    """The reference's window attention (utils/model.py:14-31: key k visible to query q iff 0 <= q - k <=
+    window, scale 1/sqrt(64)) as masked SDPA on [B, T, H, D]: flex_attention does not lower on CPU."""
+    t = q.shape[1]
+    i = torch.arange(t)
+    mask = (i[:, None] >= i[None, :]) & (i[:, None] - i[None, :] <= window)
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), attn_mask=mask).transpose(1, 2)
+
+
+REF_DIR = ROOT / 'baseline' / '_ref'
+
+
+def reference_sample(steps: int = 1, length: int = SEQ):
+    """Time the reference's own ES update on the host cores: train/val/eggroll.py Eggroll.step (its
+    population_loss, offsets into the fixed N(0, 1) buffer, z-score fitness, reconstruction and
+    torch.optim.AdamW) from the installed baseline/_ref, on one sequence with two antithetic pairs
+    (4 members x `length` tokens per step, CHUNK = 1; one pair would z-score a single difference). Only the attention primitive is swapped, for
+    the identical masked SDPA, and population_loss runs eagerly (Inductor's CPU lowering of
+    flex_attention fails). Falls back to the CPU restatement in oracle/ when baseline/_ref is absent.
+    Returns (member-tokens per step, seconds per step, cores, kind, sample)."""
     from noise_b200.data import zipf_tokens
-    from oracle import eggroll as oe
-    from oracle import model as om
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    params = om.make_params(0)
     rows = zipf_tokens(1, length + 1, seed=1)
-    draws, sign = oe.member_draws(list(range(members)), members // 2, 1e-3, 0, 1)
+    x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
     times = []
+    if (REF_DIR / 'train' / 'val' / 'eggroll.py').exists():
+        sys.path.insert(0, str(REF_DIR))
+        import train.val.eggroll as eg
+        import utils.model as um
+        um.attention = eg.attention = sdpa_window
+        eg.CHUNK = 1
+        model = eg.make_model(torch.device('cpu'), eg.SEED)
+        opt = torch.optim.AdamW(model.parameters(), lr=eg.LR, betas=eg.BETAS, eps=1e-8, weight_decay=0.0)
+        es = eg.Eggroll(model, 2)
+        es.loss = eg.population_loss
+        for step in range(1, steps + 1):
+            t0 = time.perf_counter()
+            es.step(x, y, opt, step)
+            times.append(time.perf_counter() - t0)
+        sample = (f'reference Eggroll.step (baseline/_ref, fp32 CPU): 2 pairs = 4 members x 1 sequence x {length} '
+                  'tokens, z-score fitness, reconstruction, AdamW over all 37.7M parameters')
+        return 4 * length, times, cores, 'reference', sample
+    from oracle import eggroll as oe
+    from oracle import model as om
+    params = om.make_params(0)
+    draws, sign = oe.member_draws([0, 1], 1, 1e-3, 0, 1)
     with torch.no_grad():
         for _ in range(steps):
             t0 = time.perf_counter()
-            om.population_losses(params, draws, sign, rows[:, :-1], rows[:, 1:])
+            om.population_losses(params, draws, sign, x, y)
             times.append(time.perf_counter() - t0)
-    return members * length, times, cores
+    sample = f'2 members x 1 sequence x {length} tokens of the rank-1 population forward (fp32 CPU oracle port)'
+    return 2 * length, times, cores, 'port', sample
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    sample = f'{2} members x 1 sequence x {SEQ} tokens of the rank-1 population forward (fp32 CPU oracle port)'
-    tok, times, cores = reference_sample(2, SEQ, args.warmup + args.steps)
+    tok, times, cores, kind, sample = reference_sample(args.warmup + args.steps, SEQ)
     timed = times[args.warmup:] or times
     per_step = sum(timed) / len(timed)
     value = tok / per_step
@@ -149,7 +186,7 @@ def run_reference(args, rank, world):
         'warmup': args.warmup, 'ms_per_step': per_step * 1e3, 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic Zipf(1.1) tokens, seed-0 random init',
         'config': workload_config(world, args),
-        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port', 'sample': sample},
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': kind, 'sample': sample},
         'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
@@ -287,9 +324,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tok, times, cores = reference_sample(2, SEQ, 2)
-        cpu = {'value': tok / min(times), 'unit': UNIT, 'cores': cores, 'kind': 'port',
-               'sample': '2 members x 1 sequence x 2048 tokens of the rank-1 population forward (fp32 CPU oracle port)'}
+        tok, times, cores, kind, sample = reference_sample(3, SEQ)
+        cpu = {'value': tok / min(times[1:]), 'unit': UNIT, 'cores': cores, 'kind': kind, 'sample': sample}
 
     if rank == 0:
         clk = clocks.summary()

@@ -698,14 +698,21 @@ using EpiMlpOutDirect = EpiMlpOutT<true>;
 
 // Head: soft-capped logits of the whole vocabulary, reduced on the fly to the row's cross-entropy
 // pieces. |z| <= 15 after the soft cap, so sum exp(z - 15) needs no running maximum.
+// kF32: the GEMM reads the fp32 final stream and the fp32 lm_head master through kind::tf32 MMAs (the
+// direct reruns' head, which train/val/run.py:272-278 runs in float32 with autocast off); otherwise
+// the bf16 stream copy and the packed bf16 head (the population forward's autocast head).
 // ---------------------------------------------------------------------------------------------
-struct EpiHead {
-  struct Params {
-    PopCtx ctx;
-    const float* stats;  // stats_a: sum x^2, x.b_head
-    float* part;         // [rows][2][2]: sum exp(z - 15), z[target] (0 if not in this half)
-    float* logits;       // [rows, 4096] raw logits before the soft cap (capture only), or nullptr
-  };
+struct HeadParams {
+  PopCtx ctx;
+  const float* stats;  // stats_a: sum x^2, x.b_head
+  float* part;         // [rows][2][2]: sum exp(z - 15), z[target] (0 if not in this half)
+  float* logits;       // [rows, 4096] raw logits before the soft cap (capture only), or nullptr
+};
+
+template <bool kF32>
+struct EpiHeadT {
+  static constexpr bool kTf32 = kF32;
+  using Params = HeadParams;
   static constexpr int kSmemBytes = WarpVecs<1>::kBytes;
   static constexpr bool kInterleaveN = false;
   const Params& p;
@@ -714,7 +721,7 @@ struct EpiHead {
   RowInfo ri;
   float inv, c2, se, zt;
 
-  __device__ EpiHead(const Params& p_, uint8_t* smem, int ew, int lane_)
+  __device__ EpiHeadT(const Params& p_, uint8_t* smem, int ew, int lane_)
       : p(p_), vec(reinterpret_cast<float*>(smem) + ew * 128), lane(lane_), half(ew >> 2) {}
 
   __device__ void begin_mtile(int, int row) {
@@ -762,5 +769,8 @@ struct EpiHead {
     *reinterpret_cast<float2*>(p.part + ((size_t)row * 2 + half) * 2) = make_float2(se, zt);
   }
 };
+
+using EpiHead = EpiHeadT<false>;
+using EpiHeadF32 = EpiHeadT<true>;
 
 }  // namespace noise

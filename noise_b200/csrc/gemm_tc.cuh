@@ -24,6 +24,8 @@
 //   __device__ void group(int row, int col, float (&v)[64])        64 consecutive columns of `row`
 //   __device__ void end_mtile(int m_tile, int n_tile, int row)     once per unit (n_tile = last one)
 // Optional:
+//   static constexpr bool kTf32;                     true: A and B are fp32 in HBM and the MMAs run
+//                                                    kind::tf32 (32 K elements per 128-byte row)
 //   __device__ void finish()                                       once, after the last unit
 //   __device__ void next_unit(int m_tile, int n_begin)             at the start of each unit: the 128-row
 //                  tile and first N tile of this CTA's next unit (m_tile = -1: none), for prefetches
@@ -66,17 +68,24 @@ template <class E>
 struct HasNextUnit<E, std::void_t<decltype(&E::next_unit)>> : std::true_type {};
 
 template <class E, class = void>
+struct OperandTf32 : std::false_type {};
+template <class E>
+struct OperandTf32<E, std::void_t<decltype(E::kTf32)>> : std::integral_constant<bool, E::kTf32> {};
+
+template <class E, class = void>
 struct HasFinish : std::false_type {};
 template <class E>
 struct HasFinish<E, std::void_t<decltype(&E::finish)>> : std::true_type {};
 
-template <int kStages>
+// Tiles are 128 bytes of K per row: 64 bf16 or 32 fp32 (tf32) elements; one MMA consumes 32 bytes of K
+// (K = 16 bf16 or K = 8 tf32), so a stage is always 4 MMAs.
+template <int kStages, int kElemBytes = 2>
 struct GemmLayout {
-  static constexpr int BM = 128, BN = 256, BK = 64;
+  static constexpr int BM = 128, BN = 256, BK = 128 / kElemBytes;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
-  static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kABytes = BM * 128;
+  static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kCoreBytes = kStages * kStageBytes + kBarrierBytes;
@@ -86,7 +95,8 @@ template <class Epi, int kStages>
 __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmShape shape, const __grid_constant__ typename Epi::Params ep) {
-  using L = GemmLayout<kStages>;
+  constexpr bool kTf32 = OperandTf32<Epi>::value;
+  using L = GemmLayout<kStages, kTf32 ? 4 : 2>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
@@ -163,7 +173,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = make_idesc(1, L::BM, L::BN);
+      const uint32_t idesc = make_idesc(kTf32 ? 2 : 1, L::BM, L::BN);
       uint32_t stage = 0, phase = 0, t = 0;
       bool ok = true;
       const int units = TileUnit<Epi::kInterleaveN>::count(shape);
@@ -186,8 +196,10 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
             const uint64_t da = smem_desc_sw128(sA + stage * L::kABytes);
             const uint64_t db = smem_desc_sw128(sB + stage * L::kBBytes);
 #pragma unroll
-            for (int k = 0; k < L::BK / 16; ++k)
-              tc_mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA: descriptor start + 2 (16-byte units)
+              if constexpr (kTf32) tc_mma_tf32(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+              else tc_mma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
             tc_commit(&empty[stage]);
             if (++stage == kStages) stage = 0, phase ^= 1;
           }
@@ -277,13 +289,16 @@ template <class Epi, int kStages>
 int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, int ldb,
                    const typename Epi::Params& ep, int* status, cudaStream_t stream, int kind = kKindOther,
                    int max_ctas = 0) {
-  using L = GemmLayout<kStages>;
+  constexpr bool kTf32 = OperandTf32<Epi>::value;
+  constexpr int kElem = kTf32 ? 4 : 2;
+  using L = GemmLayout<kStages, kElem>;
+  const CUtensorMapDataType dt = kTf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   if (M <= 0 || N <= 0 || K <= 0 || M % L::BM || N % L::BN || K % L::BK) return kStatusBadArgument;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) return kStatusBadArgument;
-  if ((lda * 2) % 16 || (ldb * 2) % 16 || lda < K || ldb < K) return kStatusBadArgument;
+  if (((int64_t)lda * kElem) % 16 || ((int64_t)ldb * kElem) % 16 || lda < K || ldb < K) return kStatusBadArgument;
   CUtensorMap ta, tb;
-  if (make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, L::BM, L::BK)) return kStatusBadArgument;
-  if (make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, L::BN, L::BK)) return kStatusBadArgument;
+  if (make_tmap_2d(&ta, A, dt, kElem, M, K, lda, L::BM, L::BK)) return kStatusBadArgument;
+  if (make_tmap_2d(&tb, B, dt, kElem, N, K, ldb, L::BN, L::BK)) return kStatusBadArgument;
   GemmShape shape{M, N, K, M / L::BM, N / L::BN, K / L::BK, status};
   const int smem = 1024 + L::kCoreBytes + Epi::kSmemBytes;
   static bool configured = false;  // one instantiation = one kernel

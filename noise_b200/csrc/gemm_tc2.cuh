@@ -256,8 +256,11 @@ struct PrefersPair<E, std::void_t<decltype(E::kPair)>> : std::integral_constant<
 template <class Epi, int kSingleStages>
 int launch_gemm(const void* A, const void* B, int M, int N, int K, int lda, int ldb, const typename Epi::Params& ep,
                 int* status, cudaStream_t stream, int kind) {
-  if (PrefersPair<Epi>::value && M % 256 == 0)
-    return launch_gemm_tc2<Epi, kPairStages, kPairAccs>(A, B, M, N, K, lda, ldb, ep, status, stream, kind);
+  // only bf16 epilogues that ask for it instantiate the pair engine (it has no tf32 operand mode)
+  if constexpr (PrefersPair<Epi>::value && !OperandTf32<Epi>::value) {
+    if (M % 256 == 0)
+      return launch_gemm_tc2<Epi, kPairStages, kPairAccs>(A, B, M, N, K, lda, ldb, ep, status, stream, kind);
+  }
   return launch_gemm_tc<Epi, kSingleStages>(A, B, M, N, K, lda, ldb, ep, status, stream, kind);
 }
 

@@ -449,8 +449,10 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
       return rc;
     if (cap && !copy(cap->hidden + (size_t)l * rows * kHidden, w.hidden, rows * kHidden * 2)) return kStatusLaunchFailed;
     const float* wg_next = (l + 1 < kLayers && has_ve(l + 1)) ? params + L.offset[tid_gate(l + 1)] : nullptr;
-    EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next,
-                         (cap && l == kLayers - 1) ? cap->final_x : nullptr, l};
+    // after the last block: the capture keeps the fp32 final stream; a direct rerun's fp32 head reads it
+    // from the residual buffer itself
+    float* x_final = l == kLayers - 1 ? (cap ? cap->final_x : direct ? w.x : nullptr) : nullptr;
+    EpiMlpOut::Params mp{ctx, w.x, w.xb, w.hstats, w.st_a, wte, w.inv0, lambdas, wg_next, x_final, l};
     // the direct instantiation where this block adds a draw: site 'mlp' of block `entry`, or the
     // embedding draw inside x0 in every block of a rerun from the embedding
     const bool jitter_here = direct && (l == ctx.dir.entry || ctx.dir.entry < 0);
@@ -463,9 +465,14 @@ int pop_forward_chunk(const float* params, const __nv_bfloat16* packed, const fl
       return kStatusLaunchFailed;
   }
   EpiHead::Params hp{ctx, w.st_a, w.part, cap ? cap->logits : nullptr};
-  if ((rc = launch_gemm<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
-                                                 hp, status, stream, kKindHead)))
-    return rc;
+  // direct reruns: fp32 operands (the final stream and the lm_head master) on kind::tf32, as the
+  // reference's float32 rerun head (train/val/run.py:272-278); the population forward and the capture
+  // keep the autocast head on bf16 operands
+  rc = direct ? launch_gemm<EpiHeadF32, kGemmStages>(w.x, params + L.offset[kTidHead], (int)rows, kVocab, kWidth,
+                                                      kWidth, kWidth, hp, status, stream, kKindHead)
+              : launch_gemm<EpiHead, kGemmStages>(w.xb, packed + kPackHead, (int)rows, kVocab, kWidth, kWidth, kWidth,
+                                                  hp, status, stream, kKindHead);
+  if (rc) return rc;
   {
     LaunchScope scope(kKindLoss, stream);
     if (direct || cap)

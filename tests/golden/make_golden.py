@@ -23,6 +23,9 @@ on CPU in float32 and saves their outputs as small .npz fixtures beside this scr
   local.npz        train/val/run.py DUST.local_errors for each kind (q, k, v, gate, ve) with injected
                    draws and seeded hub targets (LOCAL_CASES), plus the first block's reassembled
                    gradient per kind.
+  dust_bf16.npz,   the direct_errors and local_errors cases again with the reference's estimator set
+  local_bf16.npz   to its GPU precision (bfloat16 draws, rewards and autocast; float32 rerun head):
+                   the spread between the reference's own two precisions, the floor for any bf16 path.
   memory.npz       train/val/run.py credit memory: remember / memory_matrix / retrieve / calibrate on
                    seeded estimates keyed by the real head error, and direct_errors with retrievals
                    (MEMORY_SITES), sampled.
@@ -79,10 +82,16 @@ def main():
     ap.add_argument('--only-optim', action='store_true')
     ap.add_argument('--only-local', action='store_true')
     ap.add_argument('--only-memory', action='store_true')
+    ap.add_argument('--only-bf16', action='store_true',
+                    help='dust_bf16.npz and local_bf16.npz: the reference at its GPU precision')
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
     if args.only_dust:
         dust_golden(args.reference)
+        raise SystemExit
+    if args.only_bf16:
+        dust_golden(args.reference, bf16=True)
+        local_golden(args.reference, bf16=True)
         raise SystemExit
     if args.only_optim:
         optim_golden()
@@ -200,9 +209,11 @@ def injector(run, est):
         pats, offs = od.frame(SEED, STEP, sid, cycles, d, b_, t_)
         idx = chunk * n + np.arange(n)
         signs = od.draw_signs(SEED, STEP, sid, idx, b_, t_)
-        est.frames[site] = (pats, offs)
+        # frames and signs in the estimator's draw dtype, as DUST.signs makes them (float32 on CPU)
+        est.frames[site] = (torch.as_tensor(pats).to(est.dtype), offs)
+        sg = torch.as_tensor(signs).to(est.dtype)
         orig = est.signs
-        est.signs = lambda *shape, shared=False: signs[..., None] if shape == (n, b_, t_, 1) else orig(*shape, shared=shared)
+        est.signs = lambda *shape, shared=False: sg[..., None] if shape == (n, b_, t_, 1) else orig(*shape, shared=shared)
         try:
             a = run.DUST.orthogonal_noise(est, site, draws, chunk, n, b_, t_, d, dtype)
         finally:
@@ -224,9 +235,10 @@ def local_targets(b: int, t: int, layers: int = 8) -> dict:
     return {i: torch.randn(b, t, 512, generator=g) * 0.01 for i in range(layers)}
 
 
-def local_golden(reference):
+def local_golden(reference, bf16: bool = False):
     """DUST.local_errors (train/val/run.py:391-463) per kind with injected draws and seeded targets,
-    and each kind's reassembled gradient of its first block."""
+    and each kind's reassembled gradient of its first block. bf16: the same at the reference's GPU
+    precision (bf16_precision), into local_bf16.npz."""
     torch._dynamo.config.disable = True
     import train.val.run as run
     run.attention = sdpa_window
@@ -235,6 +247,8 @@ def local_golden(reference):
     for kind, b, t, draws in LOCAL_CASES:
         model = run.make_model(torch.device('cpu'), SEED)
         est = run.DUST(model, run.recipe(0.01), SEED, 0, 1)
+        if bf16:
+            bf16_precision(est)
         rows = zipf_tokens(b, t + 1, seed=5)
         x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
         est.capture(x, y)
@@ -242,12 +256,13 @@ def local_golden(reference):
         with torch.no_grad():
             errs = est.local_errors(kind, draws, local_targets(b, t))
         for k, (site, e) in enumerate(errs.items()):
-            out[f'le_{kind}_{k}'] = e.numpy()
+            out[f'le_{kind}_{k}'] = e.float().numpy()
         site, e = next(iter(errs.items()))
-        out[f'lr_{kind}'] = est.reassemble(site, e).numpy()
+        if not bf16:
+            out[f'lr_{kind}'] = est.reassemble(site, e).numpy()
         out[f'le_{kind}_meta'] = np.array([b, t, draws])
         print('local', kind, {s: float(v.abs().mean()) for s, v in errs.items()})
-    np.savez_compressed(HERE / 'local.npz', **pack(out, samples=1024))
+    np.savez_compressed(HERE / ('local_bf16.npz' if bf16 else 'local.npz'), **pack(out, samples=1024))
 
 
 MEMORY_SITES = ['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj', 'transformer.h.6.mlp.c_fc', 'o@0']
@@ -319,8 +334,27 @@ def memory_golden(reference):
     print('memory', out['alpha'], {k: float(np.abs(v).mean()) for k, v in out.items() if k.startswith('pe_') and 'meta' not in k})
 
 
-def dust_golden(reference):
-    """DUST fixtures; only orthogonal_noise's random frames and signs are injected."""
+def bf16_precision(est):
+    """Run a DUST estimator on CPU at the reference's GPU precision: draws and rewards in bfloat16
+    (DUST.dtype) and the capture and reruns under bfloat16 autocast (DUST.autocast), the rerun head
+    still float32 as the reference's own code keeps it (train/val/run.py:272-278)."""
+    est.dtype = torch.bfloat16
+    est.autocast = lambda: torch.autocast('cpu', dtype=torch.bfloat16)
+
+
+DUST_CASES = [
+    ('writers', ['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj'], 32, 0.4, 1, 0.0),
+    ('hidden', ['transformer.h.6.mlp.c_fc'], 16, 0.4, 6, 0.0),
+    ('embed', ['transformer.wte'], 16, 0.8, None, 0.0),
+    ('hub', ['o@0'], 16, 0.4, 0, 0.3),
+    ('deep', ['transformer.h.7.attn.c_proj', 'transformer.h.7.mlp.c_proj'], 32, 0.4, 7, 0.0),
+]
+
+
+def dust_golden(reference, bf16: bool = False):
+    """DUST fixtures; only orthogonal_noise's random frames and signs are injected. bf16: the
+    direct_errors cases again at the reference's GPU precision (bf16_precision), into dust_bf16.npz:
+    the spread between the reference's own two precisions."""
     from oracle import dust as od
     torch._dynamo.config.disable = True
     import train.val.run as run
@@ -328,15 +362,28 @@ def dust_golden(reference):
     torch.manual_seed(0)
     model = run.make_model(torch.device('cpu'), SEED)
     est = run.DUST(model, run.recipe(0.01), SEED, 0, 1)
+    if bf16:
+        bf16_precision(est)
     rows = zipf_tokens(2, 129, seed=4)
     x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
     y[1, 5] = -1  # an ignored target
     est.capture(x, y)
     b, t = x.shape
     out = dict(tokens=rows.numpy().astype(np.int16), targets=y.numpy().astype(np.int64),
-               clean_loss=est.clean_loss.numpy())
+               clean_loss=est.clean_loss.float().numpy())
 
     inject = injector(run, est)
+    if bf16:
+        est.orthogonal_noise = lambda site, draws, chunk, n, b_, t_, d, dtype=None: inject(site, draws, chunk, n, b_, t_, d, dtype)
+        for name, sites, draws, sigma, entry, gamma in DUST_CASES:
+            est.frames.clear()
+            errs = est.direct_errors(sites, draws, sigma, entry, gamma, {})
+            for k, site in enumerate(sites):
+                out[f'de_{name}_{k}'] = errs[site].float().numpy()
+            out[f'de_{name}_meta'] = np.array([draws, sigma, -1 if entry is None else entry, gamma])
+        np.savez_compressed(HERE / 'dust_bf16.npz', **pack(out))
+        print('dust bf16', {k: v.shape for k, v in out.items() if k.startswith('de_')})
+        return
 
     # orthogonal_noise itself
     a = inject('transformer.h.1.mlp.c_fc', 96, 1, 16, b, t, 2048)
@@ -353,13 +400,7 @@ def dust_golden(reference):
     out['rtg_in'], out['rtg'] = rw.numpy(), run.reward_to_go(rw, 0.3).numpy()
     # direct errors through the reference's own reruns
     est.orthogonal_noise = lambda site, draws, chunk, n, b_, t_, d, dtype=None: inject(site, draws, chunk, n, b_, t_, d, dtype)
-    cases = [
-        ('writers', ['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj'], 32, 0.4, 1, 0.0),
-        ('hidden', ['transformer.h.6.mlp.c_fc'], 16, 0.4, 6, 0.0),
-        ('embed', ['transformer.wte'], 16, 0.8, None, 0.0),
-        ('hub', ['o@0'], 16, 0.4, 0, 0.3),
-    ]
-    for name, sites, draws, sigma, entry, gamma in cases:
+    for name, sites, draws, sigma, entry, gamma in DUST_CASES:
         est.frames.clear()
         errs = est.direct_errors(sites, draws, sigma, entry, gamma, {})
         for k, site in enumerate(sites):

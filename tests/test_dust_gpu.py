@@ -55,6 +55,7 @@ CASES = {
     'hidden': (['transformer.h.6.mlp.c_fc'], ['fc']),
     'embed': (['transformer.wte'], ['transformer.wte']),
     'hub': (['o@0'], ['o']),
+    'deep': (['transformer.h.7.attn.c_proj', 'transformer.h.7.mlp.c_proj'], ['attn', 'mlp']),
 }
 
 
@@ -126,9 +127,14 @@ def test_direct_errors_match_reference(env, name):
     f = env['f']
     sites, keys, draws, sigma, entry, gamma, a = _oracle_draws(env, name)
     errs = direct_errors(env['w'], env['cap'], sites, draws, sigma, entry, gamma, SEED, STEP)
+    fb = np.load(GOLDEN / 'dust_bf16.npz')
     for k, s in enumerate(sites):
         key = f'de_{name}_{k}'
         got = errs[s].cpu().double().reshape(-1)[torch.from_numpy(f[key + '__idx'])]
-        rel, cos = _rel(got, torch.from_numpy(f[key + '__val']))
-        print(name, s, 'rel', rel, 'cos', cos)
+        want = torch.from_numpy(f[key + '__val'])
+        rel, cos = _rel(got, want)
+        frel, fcos = _rel(torch.from_numpy(fb[key + '__val']), want)
+        grel, gcos = _rel(got, torch.from_numpy(fb[key + '__val']))
+        print(f'{name} {s}: vs fp32 ref rel {rel:.4f} cos {cos:.5f}; ref bf16 vs fp32 rel {frel:.4f} cos {fcos:.5f}; '
+              f'vs bf16 ref rel {grel:.4f} cos {gcos:.5f}')
         assert rel <= REL_TOL.get(name, 5e-2) and cos >= 0.995, (rel, cos)

@@ -93,10 +93,13 @@ def test_local_errors_match_reference(golden, kind):
     targets = {i: v.cuda() for i, v in _targets(b, t).items()}
     inputs = {i: LocalInputs(w, cap, i) for i in local_layers(kind)}
     errs = local_errors(w, cap, kind, draws, targets, SEED, STEP, inputs=inputs)
+    fb = np.load(GOLDEN / 'local_bf16.npz')
     for k, (site, e) in enumerate(errs.items()):
         got, want = _pick(f, f'le_{kind}_{k}', e.cpu().double().reshape(-1))
         rel, cos = _rel(got, want)
-        print(kind, site, 'rel', rel, 'cos', cos)
+        _, wb = _pick(fb, f'le_{kind}_{k}', e.cpu().double().reshape(-1))
+        frel, fcos = _rel(wb, want)
+        print(f'{kind} {site}: vs fp32 ref rel {rel:.4f} cos {cos:.5f}; ref bf16 vs fp32 rel {frel:.4f} cos {fcos:.5f}')
         assert rel <= 6e-2 and cos >= 0.998, (site, rel, cos)
     layer = local_layers(kind)[0]
     site, e = next(iter(errs.items()))
