@@ -177,12 +177,27 @@ int noise_local_errors(const NoiseLocal* spec, const float* rope, int B, int T, 
                        uint32_t seed, uint32_t step, float* errors, void* workspace, size_t ws_bytes, int* status,
                        void* stream);
 
+/* A region of the flat parameter layout: tensors [tensor_begin, tensor_end) in named_parameters order,
+ * whose optimizer buffers (gradient, moments, ANVIL rails, polar input) are region buffers: their
+ * element i holds flat index base + i (base <= the first tensor's flat offset). {0, 60, 0} is the whole
+ * buffer. The sharded update gives each rank the region of whole tensors it owns. */
+typedef struct NoiseRegion {
+  int tensor_begin, tensor_end;
+  int64_t base;
+} NoiseRegion;
+
 /* Replaces torch.optim.AdamW.step on dense gradients (the DUST estimator's; train/val/run.py:652-655):
  * grad is a full flat gradient buffer; lr_per_tensor[60] gives each tensor's learning rate, < 0
  * for tensors another optimizer owns. adam_t is the 1-based step for the bias corrections. */
 int noise_adamw_dense(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* grad,
                       const float* lr_per_tensor, float beta1, float beta2, float eps, float weight_decay, int adam_t,
                       void* stream);
+
+/* noise_adamw_dense on one region (params and packed keep the flat layout; exp_avg, exp_avg_sq and grad
+ * are region buffers). */
+int noise_adamw_region(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* grad,
+                       const NoiseRegion* region, const float* lr_per_tensor, float beta1, float beta2, float eps,
+                       float weight_decay, int adam_t, void* stream);
 
 /* ANVIL II (train/val/run.py:583-626) over the 48 block matrices in named_parameters order, split
  * around `polar` (:572-580), whose quintic maps the caller runs on x as bf16 matmuls. Buffers with
@@ -195,6 +210,16 @@ int noise_anvil_prepare(const float* grad, float* fast, float* slow, float* scra
                         float* scalars, float fast_beta, float slow_beta, float beta, float weight, void* stream);
 int noise_anvil_finish(float* params, void* packed, const float* slow, const void* update, float* energy,
                        float* partials, float* scalars, float lane_beta, float lr, float weight_decay, void* stream);
+
+/* The same three on the block matrices of one region (grad, fast, slow, scratch and x are region
+ * buffers; energy, partials and scalars are sized for the region by noise_anvil_region_sizes). */
+int noise_anvil_region_sizes(const NoiseRegion* region, int64_t* tiles, int64_t* lanes, int* matrices);
+int noise_anvil_region_prepare(const NoiseRegion* region, const float* grad, float* fast, float* slow, float* scratch,
+                               void* x, float* partials, float* scalars, float fast_beta, float slow_beta, float beta,
+                               float weight, void* stream);
+int noise_anvil_region_finish(const NoiseRegion* region, float* params, void* packed, const float* slow,
+                              const void* update, float* energy, float* partials, float* scalars, float lane_beta,
+                              float lr, float weight_decay, void* stream);
 
 /* Scratch bytes noise_fitness needs for `members` losses. */
 size_t noise_fitness_workspace_bytes(int members);
@@ -217,6 +242,15 @@ int noise_update_sum_fe_adamw(float* params, void* packed, float* exp_avg, float
                               int pairs, float grad_scale, uint32_t seed, uint32_t step, const float* lr_mult,
                               float lr, float beta1, float beta2, float eps, float weight_decay, int adam_t,
                               float* grad_out, void* stream);
+
+/* One rank's share of the reconstruction of train/val/eggroll.py:155-163 for the sharded update
+ * (reduce-scatter of partial sums instead of every rank rebuilding all directions, :156-163):
+ * g = -grad_scale * sum over d in [dir_begin, dir_begin + dir_count) of weights[d] a_d b_d^T (eps_d for
+ * the mixing scalars), every tensor, written to out starting at out_offsets[tensor] (host array of 60;
+ * NULL: the flat layout). Summing the outputs of calls over disjoint direction ranges gives the
+ * gradient that noise_update_sum_fe_adamw reconstructs. */
+int noise_sum_fe_partial(const float* weights, int pairs, int dir_begin, int dir_count, float grad_scale,
+                         uint32_t seed, uint32_t step, const int64_t* out_offsets, float* out, void* stream);
 
 /* No counterpart in the reference: noise_fitness for callers that cannot allocate device memory
  * (an FFI host with no device allocator of its own, or a process whose device memory another

@@ -58,6 +58,15 @@ SIGNATURES: dict[str, tuple] = {
     'noise_update_sum_fe_adamw': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_uint32,
                                           c_uint32, c_void_p, c_float, c_float, c_float, c_float, c_float, c_int,
                                           c_void_p, c_void_p]),
+    'noise_adamw_region': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float,
+                                   c_float, c_float, c_float, c_int, c_void_p]),
+    'noise_anvil_region_sizes': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    'noise_anvil_region_prepare': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_float, c_float, c_float, c_float, c_void_p]),
+    'noise_anvil_region_finish': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_float, c_float, c_float, c_void_p]),
+    'noise_sum_fe_partial': (c_int, [c_void_p, c_int, c_int, c_int, c_float, c_uint32, c_uint32, c_void_p, c_void_p,
+                                     c_void_p]),
     'noise_fitness_static_max_members': (c_int, []),
     'noise_fitness_static': (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     'noise_launch_count': (c_int64, []),
@@ -87,6 +96,11 @@ class NoiseLocal(ctypes.Structure):
     _fields_ = [('kind', ctypes.c_int), ('layer', ctypes.c_int), ('site', ctypes.c_uint32), ('sigma', ctypes.c_float),
                 ('gamma', ctypes.c_float)] + [(n, c_void_p) for n in ('raw', 'q', 'k', 'values', 'gate_logits', 've',
                                                                        'target', 'base')]
+
+
+class NoiseRegion(ctypes.Structure):
+    """struct NoiseRegion of include/noise_b200.h."""
+    _fields_ = [('tensor_begin', ctypes.c_int), ('tensor_end', ctypes.c_int), ('base', ctypes.c_int64)]
 
 
 class NoiseCapture(ctypes.Structure):

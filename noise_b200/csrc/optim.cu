@@ -1,5 +1,9 @@
 // Optimizer kernels for dense gradients (the DUST estimator's reassembled gradients):
 //
+// Each runs on a region of the flat layout (NoiseRegion: tensors [tensor_begin, tensor_end), their
+// optimizer buffers holding flat indices from `base` on), the whole buffer being one region; the
+// sharded update gives each rank the region of whole tensors it owns.
+//
 // noise_adamw_dense: torch.optim.AdamW over a subset of the flat parameter buffer, with one lr
 //   multiplier per tensor (train/val/run.py:643-656: embeddings x300, mixing scalars x30, the rest
 //   x1; block matrices excluded when they go to ANVIL).
@@ -41,9 +45,10 @@ struct AdamDenseParams {
   int64_t packed[kNumTensors];
   float* params;
   __nv_bfloat16* packed_w;
-  float* m;
+  float* m;           // m, v, grad: element i holds flat index base + i (a region of the flat layout)
   float* v;
   const float* grad;
+  int64_t base;
   float lr[kNumTensors];
   float beta1, beta2, eps, wd, bc1, bc2_sqrt;
 };
@@ -57,16 +62,16 @@ __global__ void __launch_bounds__(kOptBlock) adamw_dense_kernel(const __grid_con
   for (int u = 0; u < kOptPerThread; ++u) {
     const int64_t i = base + u * kOptBlock + threadIdx.x;
     if (i >= s.n) break;
-    const int64_t idx = s.offset + i;
-    const float g = p.grad[idx];
+    const int64_t idx = s.offset + i, r = idx - p.base;
+    const float g = p.grad[r];
     float w = p.params[idx];
     if (p.wd != 0.f) w *= 1.0f - lr * p.wd;
-    const float m = torch_lerp(p.m[idx], g, 1.0f - p.beta1);
-    const float v = p.v[idx] * p.beta2 + (1.0f - p.beta2) * g * g;
+    const float m = torch_lerp(p.m[r], g, 1.0f - p.beta1);
+    const float v = p.v[r] * p.beta2 + (1.0f - p.beta2) * g * g;
     w -= step * (m / (sqrtf(v) / p.bc2_sqrt + p.eps));
     p.params[idx] = w;
-    p.m[idx] = m;
-    p.v[idx] = v;
+    p.m[r] = m;
+    p.v[r] = v;
     if (p.packed[k] >= 0 && p.packed_w) p.packed_w[p.packed[k] + i] = __float2bfloat16_rn(w);
   }
 }
@@ -87,11 +92,13 @@ struct AnvilParams {
   int count, tiles, lanes;
   float* params;
   __nv_bfloat16* packed_w;
+  // grad, fast, slow, mbuf and x: element i holds flat index base + i (a region of the flat layout)
+  int64_t base;
   const float* grad;
   float* fast;
   float* slow;
   float* mbuf;                 // scratch: m (prepare), then reused
-  __nv_bfloat16* x;            // bf16 polar input / output, same layout as params
+  __nv_bfloat16* x;            // bf16 polar input / output
   float* energy;               // [lanes]
   float* partial;              // [tiles] per-tile partial sums
   float* partial2;             // [tiles]
@@ -128,7 +135,7 @@ __global__ void __launch_bounds__(kOptBlock) anvil_blend_kernel(const __grid_con
   for (int u = 0; u < kOptPerThread; ++u) {
     const int64_t i = base + u * kOptBlock + threadIdx.x;
     if (i >= n) break;
-    const int64_t idx = M.offset + i;
+    const int64_t idx = M.offset + i - p.base;
     const float g = p.grad[idx];
     const float f = torch_lerp(p.fast[idx], g, 1.0f - p.fast_beta);
     const float s = torch_lerp(p.slow[idx], g, 1.0f - p.slow_beta);
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kOptBlock) anvil_cast_kernel(const __grid_cons
   for (int u = 0; u < kOptPerThread; ++u) {
     const int64_t i = base + u * kOptBlock + threadIdx.x;
     if (i >= n) break;
-    p.x[M.offset + i] = __float2bfloat16_rn(p.mbuf[M.offset + i] / denom);
+    p.x[M.offset + i - p.base] = __float2bfloat16_rn(p.mbuf[M.offset + i - p.base] / denom);
   }
 }
 
@@ -181,7 +188,7 @@ __global__ void __launch_bounds__(kOptBlock) anvil_energy_kernel(const __grid_co
   float ss = 0.f;
   for (int j = threadIdx.x; j < len; j += blockDim.x) {
     const int64_t i = rows_are_lanes ? (int64_t)lane * M.cols + j : (int64_t)j * M.cols + lane;
-    const float u = __bfloat162float(p.x[M.offset + i]);
+    const float u = __bfloat162float(p.x[M.offset + i - p.base]);
     ss += u * u;
   }
   const float t = block_reduce_sum(ss);
@@ -199,7 +206,7 @@ __global__ void __launch_bounds__(kOptBlock) anvil_norms_kernel(const __grid_con
   for (int uu = 0; uu < kOptPerThread; ++uu) {
     const int64_t i = base + uu * kOptBlock + threadIdx.x;
     if (i >= n) break;
-    const float u = __bfloat162float(p.x[M.offset + i]);
+    const float u = __bfloat162float(p.x[M.offset + i - p.base]);
     const int lane = rows_are_lanes ? (int)(i / M.cols) : (int)(i % M.cols);
     const float g = u * rsqrtf(fmaxf(p.energy[M.lane_begin + lane], 1e-10f));
     su += u * u;
@@ -221,12 +228,12 @@ __global__ void __launch_bounds__(kOptBlock) anvil_apply_kernel(const __grid_con
   for (int uu = 0; uu < kOptPerThread; ++uu) {
     const int64_t i = base + uu * kOptBlock + threadIdx.x;
     if (i >= n) break;
-    const int64_t idx = M.offset + i;
-    const float u = __bfloat162float(p.x[idx]);
+    const int64_t idx = M.offset + i, r = idx - p.base;
+    const float u = __bfloat162float(p.x[r]);
     const int lane = rows_are_lanes ? (int)(i / M.cols) : (int)(i % M.cols);
     const float upd = u * rsqrtf(fmaxf(p.energy[M.lane_begin + lane], 1e-10f)) * ratio;
     const float w = p.params[idx];
-    const float decay = (p.slow[idx] * w >= 0.f) ? w * (p.wd * p.lr) : 0.f;
+    const float decay = (p.slow[r] * w >= 0.f) ? w * (p.wd * p.lr) : 0.f;
     const float nw = w - lr_eff * (upd + decay);
     p.params[idx] = nw;
     if (M.packed >= 0 && p.packed_w) p.packed_w[M.packed + i] = __float2bfloat16_rn(nw);
@@ -255,12 +262,14 @@ bool is_anvil_matrix(int tid) {  // transformer.h.* 2-D parameters except ve_gat
   return false;
 }
 
-AnvilParams make_anvil_params(float* params, void* packed, const float* grad, float* fast, float* slow,
-                              float* scratch, void* x, float* energy, float* partials, float* scalars) {
+// The block matrices of tensors [region.tensor_begin, region.tensor_end), in flat order.
+AnvilParams make_anvil_params(const NoiseRegion& region, float* params, void* packed, const float* grad, float* fast,
+                              float* slow, float* scratch, void* x, float* energy, float* partials, float* scalars) {
   static const ParamLayout L = make_param_layout();
   AnvilParams p{};
+  p.base = region.base;
   int tiles = 0, lanes = 0;
-  for (int tid = 0; tid < kNumTensors; ++tid) {
+  for (int tid = region.tensor_begin; tid < region.tensor_end; ++tid) {
     if (!is_anvil_matrix(tid)) continue;
     AnvilMatrix& M = p.m[p.count++];
     M.offset = L.offset[tid];
@@ -292,14 +301,23 @@ AnvilParams make_anvil_params(float* params, void* packed, const float* grad, fl
 
 using namespace noise;
 
-extern "C" int noise_adamw_dense(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* grad,
-                                 const float* lr_per_tensor, float beta1, float beta2, float eps, float weight_decay,
-                                 int adam_t, void* stream) {
-  if (!params || !exp_avg || !exp_avg_sq || !grad || !lr_per_tensor || adam_t <= 0) return kStatusBadArgument;
+static const NoiseRegion kAllTensors = {0, kNumTensors, 0};
+
+static bool region_ok(const NoiseRegion* r) {
+  static const ParamLayout L = make_param_layout();
+  if (!r || r->tensor_begin < 0 || r->tensor_end > kNumTensors || r->tensor_begin > r->tensor_end) return false;
+  return r->tensor_begin == r->tensor_end || r->base <= L.offset[r->tensor_begin];
+}
+
+extern "C" int noise_adamw_region(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* grad,
+                                  const NoiseRegion* region, const float* lr_per_tensor, float beta1, float beta2,
+                                  float eps, float weight_decay, int adam_t, void* stream) {
+  if (!params || !exp_avg || !exp_avg_sq || !grad || !lr_per_tensor || adam_t <= 0 || !region_ok(region))
+    return kStatusBadArgument;
   static const ParamLayout L = make_param_layout();
   AdamDenseParams p{};
   int tiles = 0;
-  for (int tid = 0; tid < kNumTensors; ++tid) {
+  for (int tid = region->tensor_begin; tid < region->tensor_end; ++tid) {
     if (lr_per_tensor[tid] < 0.f) continue;  // tensors another optimizer owns
     TensorSpan& s = p.t[p.count];
     s.offset = L.offset[tid];
@@ -317,6 +335,7 @@ extern "C" int noise_adamw_dense(float* params, void* packed, float* exp_avg, fl
   p.m = exp_avg;
   p.v = exp_avg_sq;
   p.grad = grad;
+  p.base = region->base;
   p.beta1 = beta1, p.beta2 = beta2, p.eps = eps, p.wd = weight_decay;
   p.bc1 = (float)(1.0 - pow((double)beta1, adam_t));
   p.bc2_sqrt = (float)sqrt(1.0 - pow((double)beta2, adam_t));
@@ -326,20 +345,34 @@ extern "C" int noise_adamw_dense(float* params, void* packed, float* exp_avg, fl
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
 
-extern "C" int noise_anvil_sizes(int64_t* tiles, int64_t* lanes, int* matrices) {
-  AnvilParams p = make_anvil_params(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-                                    nullptr);
+extern "C" int noise_adamw_dense(float* params, void* packed, float* exp_avg, float* exp_avg_sq, const float* grad,
+                                 const float* lr_per_tensor, float beta1, float beta2, float eps, float weight_decay,
+                                 int adam_t, void* stream) {
+  return noise_adamw_region(params, packed, exp_avg, exp_avg_sq, grad, &kAllTensors, lr_per_tensor, beta1, beta2, eps,
+                            weight_decay, adam_t, stream);
+}
+
+extern "C" int noise_anvil_region_sizes(const NoiseRegion* region, int64_t* tiles, int64_t* lanes, int* matrices) {
+  if (!region_ok(region) || !tiles || !lanes || !matrices) return kStatusBadArgument;
+  AnvilParams p = make_anvil_params(*region, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                    nullptr, nullptr);
   *tiles = p.tiles;
   *lanes = p.lanes;
   *matrices = p.count;
   return kStatusOk;
 }
 
-extern "C" int noise_anvil_prepare(const float* grad, float* fast, float* slow, float* scratch, void* x,
-                                   float* partials, float* scalars, float fast_beta, float slow_beta, float beta,
-                                   float weight, void* stream) {
-  if (!grad || !fast || !slow || !scratch || !x || !partials || !scalars) return kStatusBadArgument;
-  AnvilParams p = make_anvil_params(nullptr, nullptr, grad, fast, slow, scratch, x, nullptr, partials, scalars);
+extern "C" int noise_anvil_sizes(int64_t* tiles, int64_t* lanes, int* matrices) {
+  return noise_anvil_region_sizes(&kAllTensors, tiles, lanes, matrices);
+}
+
+extern "C" int noise_anvil_region_prepare(const NoiseRegion* region, const float* grad, float* fast, float* slow,
+                                          float* scratch, void* x, float* partials, float* scalars, float fast_beta,
+                                          float slow_beta, float beta, float weight, void* stream) {
+  if (!grad || !fast || !slow || !scratch || !x || !partials || !scalars || !region_ok(region))
+    return kStatusBadArgument;
+  AnvilParams p = make_anvil_params(*region, nullptr, nullptr, grad, fast, slow, scratch, x, nullptr, partials, scalars);
+  if (p.count == 0) return kStatusOk;
   p.fast_beta = fast_beta, p.slow_beta = slow_beta, p.beta = beta, p.weight = weight;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   LaunchScope scope(kKindUpdate, s);
@@ -349,12 +382,21 @@ extern "C" int noise_anvil_prepare(const float* grad, float* fast, float* slow, 
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
 }
 
-extern "C" int noise_anvil_finish(float* params, void* packed, const float* slow, const void* update, float* energy,
-                                  float* partials, float* scalars, float lane_beta, float lr, float weight_decay,
-                                  void* stream) {
-  if (!params || !slow || !update || !energy || !partials || !scalars) return kStatusBadArgument;
-  AnvilParams p = make_anvil_params(params, packed, nullptr, nullptr, const_cast<float*>(slow), nullptr,
+extern "C" int noise_anvil_prepare(const float* grad, float* fast, float* slow, float* scratch, void* x,
+                                   float* partials, float* scalars, float fast_beta, float slow_beta, float beta,
+                                   float weight, void* stream) {
+  return noise_anvil_region_prepare(&kAllTensors, grad, fast, slow, scratch, x, partials, scalars, fast_beta,
+                                    slow_beta, beta, weight, stream);
+}
+
+extern "C" int noise_anvil_region_finish(const NoiseRegion* region, float* params, void* packed, const float* slow,
+                                         const void* update, float* energy, float* partials, float* scalars,
+                                         float lane_beta, float lr, float weight_decay, void* stream) {
+  if (!params || !slow || !update || !energy || !partials || !scalars || !region_ok(region))
+    return kStatusBadArgument;
+  AnvilParams p = make_anvil_params(*region, params, packed, nullptr, nullptr, const_cast<float*>(slow), nullptr,
                                     const_cast<void*>(update), energy, partials, scalars);
+  if (p.count == 0) return kStatusOk;
   p.lane_beta = lane_beta, p.lr = lr, p.wd = weight_decay;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   LaunchScope scope(kKindUpdate, s);
@@ -363,4 +405,11 @@ extern "C" int noise_anvil_finish(float* params, void* packed, const float* slow
   anvil_scalar_kernel<<<1, kMaxMatrices, 0, s>>>(p, 1);
   anvil_apply_kernel<<<p.tiles, kOptBlock, 0, s>>>(p);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+extern "C" int noise_anvil_finish(float* params, void* packed, const float* slow, const void* update, float* energy,
+                                  float* partials, float* scalars, float lane_beta, float lr, float weight_decay,
+                                  void* stream) {
+  return noise_anvil_region_finish(&kAllTensors, params, packed, slow, update, energy, partials, scalars, lane_beta, lr,
+                                   weight_decay, stream);
 }

@@ -1,4 +1,4 @@
-// Update reconstruction fused with AdamW.
+// Update reconstruction fused with AdamW, and its partial form for the sharded update.
 //
 // For every parameter tensor, the estimated gradient of train/val/eggroll.py:155-166,
 //     g = -scale * sum_d w_d a_d b_d^T     (matrices and embeddings: rank-1 factors a_d, b_d)
@@ -6,6 +6,9 @@
 // is accumulated tile by tile with the draws regenerated from the counter-based stream (no noise
 // tensor is stored), then the AdamW step of torch.optim.AdamW (decoupled decay, m lerp, v update,
 // bias-corrected step) is applied to the tile, and the packed bf16 GEMM copy is refreshed.
+//
+// noise_sum_fe_partial writes g alone for a range of directions, each tensor at a caller-given offset:
+// a rank's share of the sum, laid out for the reduce-scatter of the sharded update.
 //
 // Tiles are 128 x 128; 256 threads hold 8 rows x 8 columns each (rows ty + 16 i, columns
 // 4 tx + 64 j .. +3), so global reads and writes are 256-byte contiguous per half-warp. Draws for 8
@@ -19,6 +22,7 @@ namespace noise {
 
 struct UpdTensor {
   int64_t offset;   // in the flat master buffer
+  int64_t out;      // where g of this tensor starts in grad_out
   int64_t packed;   // packed bf16 destination offset, or -1
   int rows, cols;   // cols == 1: a vector of eps draws
   int tile_begin;   // first tile index of this tensor
@@ -35,7 +39,7 @@ struct UpdParams {
   float* grad_out;
   const float* weights;
   const float* lr_mult;  // per-tensor lr multiplier or nullptr
-  int pairs;
+  int dir_begin, dir_end;  // the directions contracted: weights[d] for d in [dir_begin, dir_end)
   float scale;
   PhiloxKey key;
   float lr, beta1, beta2, eps, weight_decay, bc1, bc2_sqrt;
@@ -63,7 +67,7 @@ __global__ void __launch_bounds__(256) sum_fe_adamw_kernel(const __grid_constant
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  for (int d0 = 0; d0 < p.pairs; d0 += kUpdBatch) {
+  for (int d0 = p.dir_begin; d0 < p.dir_end; d0 += kUpdBatch) {
     __syncthreads();
     {
       // 8 directions x (32 a-blocks + 32 b-blocks) = 512 Philox blocks, two per thread
@@ -71,7 +75,7 @@ __global__ void __launch_bounds__(256) sum_fe_adamw_kernel(const __grid_constant
         const int dd = q >> 6, which = (q >> 5) & 1, blk = q & 31;
         const int d = d0 + dd;
         float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (d < p.pairs) {
+        if (d < p.dir_end) {
           if (which == 0) {
             const int e0 = r0 + 4 * blk;
             if (e0 < T.rows) g = gauss4(p.key, (uint32_t)(e0 >> 2), (uint32_t)ti, 0, (uint32_t)d);
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(256) sum_fe_adamw_kernel(const __grid_constant
         }
         (which == 0 ? sa : sb)[dd][blk] = g;
       }
-      if (threadIdx.x < kUpdBatch) sw[threadIdx.x] = d0 + threadIdx.x < p.pairs ? p.weights[d0 + threadIdx.x] : 0.f;
+      if (threadIdx.x < kUpdBatch) sw[threadIdx.x] = d0 + threadIdx.x < p.dir_end ? p.weights[d0 + threadIdx.x] : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(256) sum_fe_adamw_kernel(const __grid_constant
       for (int u = 0; u < 4; ++u) {
         if (u >= nv) break;
         const float g = -p.scale * acc[i][4 * jj + u];
-        if (p.grad_out) p.grad_out[idx + u] = g;
+        if (p.grad_out) p.grad_out[T.out + (idx - T.offset) + u] = g;
         if (!p.apply_adam) continue;
         float w = p.params[idx + u];
         if (p.weight_decay != 0.f) w *= 1.0f - lr * p.weight_decay;
@@ -158,20 +162,15 @@ static int64_t packed_offset_of(int tid) {
   return -1;
 }
 
-extern "C" int noise_update_sum_fe_adamw(float* params, void* packed, float* exp_avg, float* exp_avg_sq,
-                                         const float* weights, int pairs, float grad_scale, uint32_t seed,
-                                         uint32_t step, const float* lr_mult, float lr, float beta1, float beta2,
-                                         float eps, float weight_decay, int adam_t, float* grad_out, void* stream) {
-  if (!params || !weights || pairs <= 0) return kStatusBadArgument;
-  const bool adam = adam_t > 0;
-  if (adam && (!exp_avg || !exp_avg_sq)) return kStatusBadArgument;
-  if (!adam && !grad_out) return kStatusBadArgument;
+// The tensor table of every parameter: tiles, packed offsets, and g's destination (out_offsets[tid], or
+// the flat layout when null).
+static int build_tensors(UpdParams& p, const int64_t* out_offsets) {
   static const ParamLayout L = make_param_layout();
-  UpdParams p{};
   int tiles = 0;
   for (int i = 0; i < kNumTensors; ++i) {
     UpdTensor& t = p.t[i];
     t.offset = L.offset[i];
+    t.out = out_offsets ? out_offsets[i] : L.offset[i];
     t.rows = L.rows[i];
     t.cols = L.cols[i];
     t.packed = packed_offset_of(i);
@@ -180,6 +179,19 @@ extern "C" int noise_update_sum_fe_adamw(float* params, void* packed, float* exp
     tiles += ((t.rows + kUpdTile - 1) / kUpdTile) * t.tiles_c;
   }
   p.ntensors = kNumTensors;
+  return tiles;
+}
+
+extern "C" int noise_update_sum_fe_adamw(float* params, void* packed, float* exp_avg, float* exp_avg_sq,
+                                         const float* weights, int pairs, float grad_scale, uint32_t seed,
+                                         uint32_t step, const float* lr_mult, float lr, float beta1, float beta2,
+                                         float eps, float weight_decay, int adam_t, float* grad_out, void* stream) {
+  if (!params || !weights || pairs <= 0) return kStatusBadArgument;
+  const bool adam = adam_t > 0;
+  if (adam && (!exp_avg || !exp_avg_sq)) return kStatusBadArgument;
+  if (!adam && !grad_out) return kStatusBadArgument;
+  UpdParams p{};
+  const int tiles = build_tensors(p, nullptr);
   p.params = params;
   p.packed = reinterpret_cast<__nv_bfloat16*>(packed);
   p.exp_avg = exp_avg;
@@ -187,7 +199,7 @@ extern "C" int noise_update_sum_fe_adamw(float* params, void* packed, float* exp
   p.grad_out = grad_out;
   p.weights = weights;
   p.lr_mult = lr_mult;
-  p.pairs = pairs;
+  p.dir_begin = 0, p.dir_end = pairs;
   p.scale = grad_scale;
   p.key = PhiloxKey{seed, step};
   p.lr = lr, p.beta1 = beta1, p.beta2 = beta2, p.eps = eps, p.weight_decay = weight_decay;
@@ -198,6 +210,28 @@ extern "C" int noise_update_sum_fe_adamw(float* params, void* packed, float* exp
   } else {
     p.bc1 = 1.f, p.bc2_sqrt = 1.f;
   }
+  LaunchScope scope(kKindUpdate, reinterpret_cast<cudaStream_t>(stream));
+  sum_fe_adamw_kernel<<<tiles, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;
+}
+
+extern "C" int noise_sum_fe_partial(const float* weights, int pairs, int dir_begin, int dir_count, float grad_scale,
+                                    uint32_t seed, uint32_t step, const int64_t* out_offsets, float* out,
+                                    void* stream) {
+  if (!weights || !out || pairs <= 0 || dir_begin < 0 || dir_count < 0 || dir_begin + dir_count > pairs)
+    return kStatusBadArgument;
+  if (out_offsets)
+    for (int i = 0; i < kNumTensors; ++i)
+      if (out_offsets[i] < 0) return kStatusBadArgument;
+  UpdParams p{};
+  const int tiles = build_tensors(p, out_offsets);
+  p.grad_out = out;
+  p.weights = weights;
+  p.dir_begin = dir_begin, p.dir_end = dir_begin + dir_count;
+  p.scale = grad_scale;
+  p.key = PhiloxKey{seed, step};
+  p.apply_adam = 0;
+  p.bc1 = 1.f, p.bc2_sqrt = 1.f;
   LaunchScope scope(kKindUpdate, reinterpret_cast<cudaStream_t>(stream));
   sum_fe_adamw_kernel<<<tiles, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? kStatusOk : kStatusLaunchFailed;

@@ -10,6 +10,7 @@ equals polar applied to the transpose.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -55,24 +56,43 @@ class DenseGrad:
             off += k
 
 
-class AdamWDense:
-    """AdamW on dense gradients for the non-ANVIL tensors, lr = base lr x adam_scale(name)."""
+def whole_region() -> _lib.NoiseRegion:
+    """The region of every tensor: the flat buffer itself."""
+    return _lib.NoiseRegion(0, len(PARAM_SPECS), 0)
 
-    def __init__(self, w: Weights, lr: float, betas, eps=1e-8, weight_decay=0.0):
+
+def region_numel(region: _lib.NoiseRegion) -> int:
+    """Elements a region buffer needs: from `base` to the end of its last tensor."""
+    end = sum(math.prod(s) for _, s in PARAM_SPECS[:region.tensor_end])
+    return end - region.base
+
+
+class AdamWDense:
+    """AdamW on dense gradients for the non-ANVIL tensors, lr = base lr x adam_scale(name).
+
+    On a region (noise_b200.shard), only the region's tensors are stepped and the moments are region
+    buffers; `names` limits the tensors (all non-ANVIL ones by default)."""
+
+    def __init__(self, w: Weights, lr: float, betas, eps=1e-8, weight_decay=0.0, region=None, names=None,
+                 scale=adam_scale):
         self.w = w
-        self.m = torch.zeros_like(w.flat)
-        self.v = torch.zeros_like(w.flat)
+        self.region = region or whole_region()
+        n = region_numel(self.region)
+        self.m = torch.zeros(n, dtype=torch.float32, device=w.device)
+        self.v = torch.zeros(n, dtype=torch.float32, device=w.device)
         self.t = 0
         self.param_groups = []
         groups = {}
-        for n, s in PARAM_SPECS:
-            if not is_anvil_matrix(n, s):
-                groups.setdefault(adam_scale(n), []).append(n)
-        for scale, names in groups.items():
-            self.param_groups.append(dict(names=names, lr=lr * scale, betas=tuple(betas), eps=eps,
+        for nm, sh in PARAM_SPECS:
+            if (names is None and not is_anvil_matrix(nm, sh)) or (names is not None and nm in names):
+                groups.setdefault(scale(nm), []).append(nm)
+        for sc, group in groups.items():
+            self.param_groups.append(dict(names=group, lr=lr * sc, betas=tuple(betas), eps=eps,
                                           weight_decay=weight_decay))
 
-    def step(self, grad: DenseGrad):
+    def step(self, grad):
+        """grad: a DenseGrad (whole buffer) or a region buffer tensor."""
+        flat = grad.flat if isinstance(grad, DenseGrad) else grad
         self.t += 1
         lrs = [-1.0] * len(PARAM_SPECS)
         index = {n: i for i, (n, _) in enumerate(PARAM_SPECS)}
@@ -81,17 +101,20 @@ class AdamWDense:
                 lrs[index[n]] = float(g['lr'])
         lr_arr = (ctypes.c_float * len(lrs))(*lrs)
         g0 = self.param_groups[0]
-        _lib.call('noise_adamw_dense', self.w.flat.data_ptr(), self.w.packed.data_ptr(), self.m.data_ptr(),
-                  self.v.data_ptr(), grad.flat.data_ptr(), ctypes.addressof(lr_arr), float(g0['betas'][0]),
-                  float(g0['betas'][1]), float(g0['eps']), float(g0['weight_decay']), self.t, _stream(self.w.device))
+        _lib.call('noise_adamw_region', self.w.flat.data_ptr(), self.w.packed.data_ptr(), self.m.data_ptr(),
+                  self.v.data_ptr(), flat.data_ptr(), ctypes.byref(self.region), ctypes.addressof(lr_arr),
+                  float(g0['betas'][0]), float(g0['betas'][1]), float(g0['eps']), float(g0['weight_decay']), self.t,
+                  _stream(self.w.device))
 
 
 class Anvil:
-    """ANVIL II (modded-nanogpt PR #360) as in train/val/run.py:583-626."""
+    """ANVIL II (modded-nanogpt PR #360) as in train/val/run.py:583-626, on the block matrices of a
+    region (all 48 by default)."""
 
     def __init__(self, w: Weights, lr: float, weight_decay: float, steps: int, lane_beta=0.9, beta_min=0.85,
-                 beta_max=0.93, slow_beta=0.98, fast_beta=0.85, fast_weight=0.4385):
+                 beta_max=0.93, slow_beta=0.98, fast_beta=0.85, fast_weight=0.4385, region=None):
         self.w = w
+        self.region = region or whole_region()
         self.param_groups = [dict(lr=lr, weight_decay=weight_decay)]
         self.total, self.warmup, self.cooldown, self.engage = (round(k * steps / RUN[0]) for k in RUN)
         self.lane_beta, self.beta_min, self.beta_max = lane_beta, beta_min, beta_max
@@ -99,20 +122,24 @@ class Anvil:
         self.t = 0
         dev = w.device
         tiles, lanes, mats = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
-        _lib.call('noise_anvil_sizes', ctypes.addressof(tiles), ctypes.addressof(lanes), ctypes.addressof(mats))
-        self.fast = torch.zeros_like(w.flat)
-        self.slow = torch.zeros_like(w.flat)
-        self.scratch = torch.zeros_like(w.flat)
-        self.x = torch.zeros(w.flat.numel(), dtype=torch.bfloat16, device=dev)
-        self.energy = torch.zeros(lanes.value, dtype=torch.float32, device=dev)
-        self.partials = torch.zeros(2 * tiles.value, dtype=torch.float32, device=dev)
-        self.scalars = torch.zeros(mats.value, dtype=torch.float32, device=dev)
-        # views of x per matrix, grouped by shape for batched maps
+        _lib.call('noise_anvil_region_sizes', ctypes.byref(self.region), ctypes.addressof(tiles),
+                  ctypes.addressof(lanes), ctypes.addressof(mats))
+        self.matrices = mats.value
+        n = region_numel(self.region)
+        self.fast = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.slow = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.scratch = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.x = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        self.energy = torch.zeros(max(1, lanes.value), dtype=torch.float32, device=dev)
+        self.partials = torch.zeros(max(1, 2 * tiles.value), dtype=torch.float32, device=dev)
+        self.scalars = torch.zeros(max(1, mats.value), dtype=torch.float32, device=dev)
+        # views of x per matrix of the region, grouped by shape for batched maps
         self.wide, self.tall, off = {}, {}, 0
-        for n, s in PARAM_SPECS:
-            k = s[0] * (s[1] if len(s) > 1 else 1)
-            if is_anvil_matrix(n, s):
-                (self.tall if s[0] > s[1] else self.wide).setdefault(s, []).append(self.x[off:off + k].view(s))
+        for tid, (nm, sh) in enumerate(PARAM_SPECS):
+            k = math.prod(sh)
+            if self.region.tensor_begin <= tid < self.region.tensor_end and is_anvil_matrix(nm, sh):
+                lo = off - self.region.base
+                (self.tall if sh[0] > sh[1] else self.wide).setdefault(sh, []).append(self.x[lo:lo + k].view(sh))
             off += k
 
     def rail_beta(self):
@@ -138,18 +165,23 @@ class Anvil:
                     v.copy_(xi)
 
     @torch.no_grad()
-    def step(self, grad: DenseGrad):
+    def step(self, grad):
+        """grad: a DenseGrad (whole buffer) or a region buffer tensor."""
+        flat = grad.flat if isinstance(grad, DenseGrad) else grad
         beta, engaged = self.rail_beta(), self.t >= self.engage
         fast_beta, weight = (self.fast_beta, self.fast_weight) if engaged else (beta, 1.0)
         dev = self.w.device
         g = self.param_groups[0]
-        _lib.call('noise_anvil_prepare', grad.flat.data_ptr(), self.fast.data_ptr(), self.slow.data_ptr(),
-                  self.scratch.data_ptr(), self.x.data_ptr(), self.partials.data_ptr(), self.scalars.data_ptr(),
-                  float(fast_beta), float(self.slow_beta), float(beta), float(weight), _stream(dev))
-        self._polar_maps()
-        _lib.call('noise_anvil_finish', self.w.flat.data_ptr(), self.w.packed.data_ptr(), self.slow.data_ptr(),
-                  self.x.data_ptr(), self.energy.data_ptr(), self.partials.data_ptr(), self.scalars.data_ptr(),
-                  float(self.lane_beta), float(g['lr']), float(g['weight_decay']), _stream(dev))
+        if self.matrices:
+            _lib.call('noise_anvil_region_prepare', ctypes.byref(self.region), flat.data_ptr(), self.fast.data_ptr(),
+                      self.slow.data_ptr(), self.scratch.data_ptr(), self.x.data_ptr(), self.partials.data_ptr(),
+                      self.scalars.data_ptr(), float(fast_beta), float(self.slow_beta), float(beta), float(weight),
+                      _stream(dev))
+            self._polar_maps()
+            _lib.call('noise_anvil_region_finish', ctypes.byref(self.region), self.w.flat.data_ptr(),
+                      self.w.packed.data_ptr(), self.slow.data_ptr(), self.x.data_ptr(), self.energy.data_ptr(),
+                      self.partials.data_ptr(), self.scalars.data_ptr(), float(self.lane_beta), float(g['lr']),
+                      float(g['weight_decay']), _stream(dev))
         self.t += 1
 
 

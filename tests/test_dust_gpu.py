@@ -1,9 +1,14 @@
 """DUST's direct-draw path on the GPU against the CPU oracle and the reference's fixtures.
 
-Tolerances: per-token rerun losses rel 2e-3 (bf16 GEMM operands vs the fp32 oracle); the error
-contraction and coordinate differences on identical inputs rtol 1e-4; the full estimate (rerun +
-contraction) against the reference's direct_errors: relative L2 error <= 5e-2 with cosine >= 0.995,
-since the per-token rewards (~1e-3) sit within a decade of bf16 rounding."""
+Tolerances: per-token rerun losses rel 2e-3 (bf16 GEMM operands in the blocks, fp32 head on tf32
+MMAs, vs the fp32 oracle); the error contraction and coordinate differences on identical inputs rtol
+1e-4; the full estimate (rerun + contraction) against the reference's float32 direct_errors
+(tests/golden/dust.npz): cosine >= 0.999 and relative L2 error <= 2e-2, unless the reference's own
+GPU precision (the same estimator with bfloat16 draws, rewards and autocast, float32 rerun head:
+tests/golden/dust_bf16.npz) is itself further from its float32 result, in which case this path must
+be at least as close as the reference's: cosine >= that floor's and relative error <= its. Only the
+MLP-hidden site (block 6, live units) has such a floor (cosine 0.9968, relative error 0.080); this
+path measures 0.9985 and 0.056 there, and 0.9999 / <= 0.016 in every other case."""
 from pathlib import Path
 
 import numpy as np
@@ -43,12 +48,6 @@ def test_capture_matches_oracle(env):
     rel, cos = _rel(cap.logits.cpu(), ocap['raw'])
     assert rel < 2e-2 and cos > 0.9998, (rel, cos)
 
-
-# Relative error of the whole estimate against the fp32 reference. The hidden site's loss differences
-# (jitter on block 6's FC pre-activation) are the smallest against the bf16 rounding of the rerun, so
-# its estimate sits at 0.05-0.06 and moves by about 0.01 under fp32-equivalent reorderings of a
-# kernel's sums (a softmax row-sum order); the other cases sit at 0.01-0.02.
-REL_TOL = {'hidden': 8e-2}
 
 CASES = {
     'writers': (['transformer.h.1.attn.c_proj', 'transformer.h.1.mlp.c_proj'], ['attn', 'mlp']),
@@ -137,4 +136,4 @@ def test_direct_errors_match_reference(env, name):
         grel, gcos = _rel(got, torch.from_numpy(fb[key + '__val']))
         print(f'{name} {s}: vs fp32 ref rel {rel:.4f} cos {cos:.5f}; ref bf16 vs fp32 rel {frel:.4f} cos {fcos:.5f}; '
               f'vs bf16 ref rel {grel:.4f} cos {gcos:.5f}')
-        assert rel <= REL_TOL.get(name, 5e-2) and cos >= 0.995, (rel, cos)
+        assert cos >= min(0.999, fcos) and rel <= max(2e-2, frel), (rel, cos, frel, fcos)

@@ -2,8 +2,14 @@
 (tests/golden/local.npz: DUST.local_errors with the same injected draws and seeded hub targets).
 
 Tolerances: processed queries within bf16 rounding (rel 1e-2 per element); clean scores relative L2
-2e-2 (bf16 q, k, values and P against fp32); the full estimate relative L2 <= 6e-2 and cosine >= 0.998
-against the reference: the GPU reruns carry bf16 operands where the CPU reference is fp32."""
+2e-2 (bf16 q, k, values and P against fp32); the full estimate against the reference's float32
+local_errors: cosine >= 0.999 and relative L2 error <= 2e-2, unless the reference's own GPU precision
+(bfloat16 draws, operands and attention outputs: tests/golden/local_bf16.npz) is further from its
+float32 result, in which case this path must be at least as close: cosine >= that floor's and
+relative error <= its. Such floors exist for q (cosine 0.9921-0.9990, relative error 0.045-0.125)
+and k (0.9701-0.9972, 0.076-0.252): the reference differences two bf16 attention outputs, while this
+path scores <target, O> in fp32 and measures cosine 0.9989-0.9995, relative error 0.032-0.048.
+Each kind's reassembled gradient: cosine >= 0.999, relative error <= 4e-2."""
 from pathlib import Path
 
 import numpy as np
@@ -100,13 +106,13 @@ def test_local_errors_match_reference(golden, kind):
         _, wb = _pick(fb, f'le_{kind}_{k}', e.cpu().double().reshape(-1))
         frel, fcos = _rel(wb, want)
         print(f'{kind} {site}: vs fp32 ref rel {rel:.4f} cos {cos:.5f}; ref bf16 vs fp32 rel {frel:.4f} cos {fcos:.5f}')
-        assert rel <= 6e-2 and cos >= 0.998, (site, rel, cos)
+        assert cos >= min(0.999, fcos) and rel <= max(2e-2, frel), (site, rel, cos, frel, fcos)
     layer = local_layers(kind)[0]
     site, e = next(iter(errs.items()))
     g = reassemble_local(w, cap, kind, layer, e, inputs[layer]).cpu().double().reshape(-1)
     rel, cos = _rel(*_pick(f, f'lr_{kind}', g))
     print(kind, 'reassembled rel', rel, 'cos', cos)
-    assert rel <= 6e-2 and cos >= 0.998, (rel, cos)
+    assert rel <= 4e-2 and cos >= 0.999, (rel, cos)
 
 
 def test_local_errors_split_into_blocks_add_up(golden):
