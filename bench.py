@@ -3,8 +3,16 @@
 
 One step = one full ES update: population forward of 1024 rank-1 antithetic members per GPU
 (512 directions per GPU, sigma 1e-3), every member on the same 8 Zipf(1.1) sequences x 2048 tokens,
-per-member CE losses, NCCL all-gather of losses (N > 1), centred-rank fitness, Sigma f eps
-reconstruction fused with AdamW (lr 1e-3), packed-weight refresh.
+per-member CE losses, NCCL all-gather of losses (N > 1), centred-rank fitness, each rank's partial
+Sigma f eps reduce-scattered, AdamW (lr 1e-3) on the owned tensors, parameter all-gather and
+packed-weight refresh.
+
+Extra keys of the same line, measured in the same process after the headline (skip: --no-extras):
+  fixed_population        BASELINE config 4: 16,384 members split over the N GPUs, ANVIL II on the
+                          block matrices + AdamW elsewhere, seconds per update (strong scaling)
+  dust                    seconds per DUST update at the speedrun recipe (5,440 draws, config 3) and at
+                          24,576 direct draws (config 5), draws split over the GPUs
+  eggroll_131072_pairs    (N >= 8) config 5's EGGROLL population: 262,144 members, one update
 
     python bench.py [--gpus N --steps K --warmup W]          # this repository's CUDA path
     python bench.py --impl reference [...]                   # the reference's own ES update on the host cores
@@ -196,6 +204,7 @@ def workload_config(world, args):
     return {'workload': 'eggroll-rank1-antithetic', 'members_per_gpu': 2 * args.pairs_per_gpu,
             'pairs': args.pairs_per_gpu * world, 'sigma': args.sigma, 'sequences_per_member': BATCH,
             'seq_len': SEQ, 'fitness': 'centered_rank', 'optimizer': 'adamw lr 1e-3 betas (0.5, 0.95)',
+            'update': 'sharded: per-rank partial sum f eps, reduce-scatter, region AdamW, parameter all-gather',
             'parallelism': f'members sharded dp{world}', 'operands': 'bf16 GEMM operands, fp32 accumulate/head/CE',
             'l2': 'inputs larger than L2 (activations streamed per chunk, GBs)'}
 
@@ -213,6 +222,8 @@ def main():
     ap.add_argument('--workload', default='eggroll', choices=['eggroll', 'dust'],
                     help='eggroll (the headline line) or dust: seconds per DUST update, a separate line')
     ap.add_argument('--dust-scale', type=float, default=0.3125, help='DUST recipe scale (1.0 = the 16k cell)')
+    ap.add_argument('--no-extras', action='store_true',
+                    help='skip the extra configurations (fixed population 16,384 with ANVIL, DUST updates)')
     args = ap.parse_args()
     rank, world, local = dist_setup()
     if args.impl == 'reference':
@@ -224,8 +235,9 @@ def main():
 
     from noise_b200 import _lib, population
     from noise_b200.data import zipf_tokens
-    from noise_b200.eggroll import BETAS, AdamW, Eggroll
+    from noise_b200.eggroll import BETAS, Eggroll
     from noise_b200.model import Weights
+    from noise_b200.shard import ShardedOptimizer
 
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
@@ -237,7 +249,7 @@ def main():
     pairs = args.pairs_per_gpu * world
     members_total = 2 * pairs
     w = Weights(dev, seed=0)
-    opt = AdamW(w, lr=1e-3, betas=BETAS)
+    opt = ShardedOptimizer(w, rank, world, kind='adamw', lr=1e-3, betas=BETAS)
     es = Eggroll(w, pairs, rank, world, sigma=args.sigma, seed=0, fitness='centered_rank', all_sequences=True)
     rows = zipf_tokens(BATCH, SEQ + 1, seed=1)
     rows_dev = rows.to(dev)
@@ -327,6 +339,15 @@ def main():
         tok, times, cores, kind, sample = reference_sample(3, SEQ)
         cpu = {'value': tok / min(times[1:]), 'unit': UNIT, 'cores': cores, 'kind': kind, 'sample': sample}
 
+    extras = {}
+    if not args.no_extras:
+        extras['fixed_population'] = fixed_population(rank, world, dev, FIXED_MEMBERS, args.sigma, barrier)
+        extras['dust'] = {f'{scale}': dust_update(rank, world, dev, scale, steps, barrier)
+                          for scale, steps in DUST_SCALES}
+        if world >= 8:
+            extras['eggroll_131072_pairs'] = fixed_population(rank, world, dev, 2 * 131072, args.sigma, barrier,
+                                                              steps=1, warmup=0, kind='adamw')
+
     if rank == 0:
         clk = clocks.summary()
         line = {
@@ -341,9 +362,99 @@ def main():
             'gpu_launches': launches, 'roofline': roofline, 'cpu_baseline': cpu,
             'clocks': {'sm_mhz': clk['sm_mhz'], 'sm_max_mhz': clk['sm_max_mhz'], 'reasons': clk['reasons']},
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+# population 16,384 split over the GPUs (strong scaling), ANVIL II on the block
+# matrices and AdamW elsewhere, the sharded update. Config 5's direct-draw population: the DUST recipe
+# scale with 24,576 draws per update; the speedrun recipe (0.3125, 5,440 draws) is config 3's.
+FIXED_MEMBERS = 16384
+DUST_SCALES = ((0.3125, 2), (1.2657, 1))
+
+
+def timed_steps(fn, steps, warmup, barrier, dev):
+    """Device time per call of fn() (CUDA events on the current stream after `warmup` untimed calls),
+    max over ranks."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        fn()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / steps
+    if torch.distributed.is_initialized():
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    return ms
+
+
+def fixed_population(rank, world, dev, members, sigma, barrier, steps=2, warmup=1, kind='anvil'):
+    """Seconds per full ES update (draw generation through the optimizer step) at a fixed population
+    split over the ranks: rank-1 antithetic members on the same 8 x 2048-token batch, centred-rank
+    fitness, the sharded update (partial Sigma f eps, reduce-scatter, region optimizer, all-gather)."""
+    from noise_b200 import _lib
+    from noise_b200.data import zipf_tokens
+    from noise_b200.dust import recipe
+    from noise_b200.eggroll import BETAS, Eggroll
+    from noise_b200.model import Weights
+    from noise_b200.shard import ShardedOptimizer
+    rec = recipe(1.0)
+    w = Weights(dev, seed=0)
+    opt = ShardedOptimizer(w, rank, world, kind=kind, lr=1e-3, betas=BETAS, anvil_lr=rec.anvil_lr,
+                           anvil_wd=rec.anvil_wd, steps=610)
+    es = Eggroll(w, members // 2, rank, world, sigma=sigma, seed=0, fitness='centered_rank', all_sequences=True)
+    rows = zipf_tokens(BATCH, SEQ + 1, seed=1).to(dev)
+    x, y = rows[:, :-1], rows[:, 1:]
+    state = {'step': 0}
+
+    def one():
+        state['step'] += 1
+        es.step(x, y, opt, state['step'])
+
+    _lib.call('noise_profile_enable', 1)
+    ms = timed_steps(one, steps, warmup, barrier, dev)
+    kinds = (ctypes_array('d', len(KINDS)), ctypes_array('q', len(KINDS)))
+    _lib.call('noise_profile_read', kinds[0].buffer_info()[0], kinds[1].buffer_info()[0], len(KINDS))
+    _lib.call('noise_profile_enable', 0)
+    calls = warmup + steps
+    tokens = members * BATCH * SEQ
+    return {'members': members, 'pairs': members // 2, 'members_per_gpu': members // world, 's_per_update': ms / 1e3,
+            'value': tokens / (ms / 1e3), 'unit': UNIT, 'steps': steps, 'warmup': warmup,
+            'optimizer': 'ANVIL II on block matrices, AdamW x300/x30/x1 elsewhere' if kind == 'anvil' else 'AdamW',
+            'update': 'sharded: per-rank partial sum f eps, reduce-scatter, region optimizer, parameter all-gather',
+            'update_ms_per_step': kinds[0][KINDS.index('update')] / calls,
+            'fitness_ms_per_step': kinds[0][KINDS.index('fitness')] / calls,
+            'scaling': 'strong'}
+
+
+def dust_update(rank, world, dev, scale, steps, barrier, warmup=1):
+    """Seconds per DUST update (train/val/run.py DUST.step with ANVIL II + AdamW) on 8 x 2048 tokens
+    copied from pinned host memory each step, the recipe's draws split over the ranks."""
+    from noise_b200.data import zipf_tokens
+    from noise_b200.dust import DUST, recipe
+    from noise_b200.model import Weights
+    from noise_b200.optim import make_optimizer
+    rec = recipe(scale)
+    w = Weights(dev, seed=0)
+    est = DUST(w, rec, 0, rank, world)
+    opt = make_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 610)
+    rows = zipf_tokens(BATCH, SEQ + 1, seed=1).pin_memory()
+    x, y = rows[:, :-1], rows[:, 1:]
+    ms = timed_steps(lambda: est.step(x, y, opt), steps, warmup, barrier, dev)
+    draws = sum(rec.writers) + sum(rec.hidden) + sum(rec.hubs) + rec.embedding + sum(rec.local.values())
+    published = DUST_PUBLISHED_8XH100.get(scale)
+    return {'recipe_scale': scale, 'draws_per_update': draws, 's_per_update': ms / 1e3, 'steps': steps,
+            'warmup': warmup, 'reference_8xh100_s_per_update': published, 'scaling': 'strong'}
 
 
 # The reference's own logs on 8xH100 (train/val/log, train/speedrun/log): seconds per DUST update.

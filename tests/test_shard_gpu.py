@@ -1,0 +1,104 @@
+"""The sharded update's kernels on one GPU: W ranks emulated in one process (each rank's partial
+reconstruction, the reduce-scatter as a sum of the partials, each rank's region optimizer on shared
+parameters) against the replicated path.
+
+1. The summed partials equal the gradient noise_update_sum_fe_adamw reconstructs from all directions
+   (rtol 1e-5: only the fp32 summation order differs).
+2. kind 'adamw', two updates: parameter changes against the replicated fused Sigma f eps + AdamW
+   kernel: relative L2 <= 1e-5 (a handful of entries whose gradient is within rounding of zero may
+   take the other sign of AdamW's near-unit step).
+3. kind 'anvil', two updates: against ANVIL II + AdamW on the whole buffer (noise_b200.optim, pinned
+   to the reference's make_optimizer by tests/test_optim_gpu.py) fed the replicated gradient: relative
+   L2 <= 2e-3 and cosine >= 0.99999 (the polar maps run in bf16, where a rounding can flip).
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SEED, PAIRS = 0, 64
+
+
+def _weights(step):
+    g = torch.Generator().manual_seed(100 + step)
+    return torch.randn(PAIRS, generator=g).cuda()
+
+
+def _rel(a, b):
+    a, b = a.double(), b.double()
+    return ((a - b).norm() / b.norm()).item(), torch.nn.functional.cosine_similarity(a, b, dim=0).item()
+
+
+def _emulate(world, kind, steps=2):
+    from noise_b200.model import Weights
+    from noise_b200.shard import ShardedOptimizer
+    w = Weights('cuda', seed=0)
+    opts = [ShardedOptimizer(w, r, world, kind=kind, anvil_lr=0.02, anvil_wd=0.01, steps=100) for r in range(world)]
+    size = opts[0].plan.size
+    for step in range(1, steps + 1):
+        fw = _weights(step)
+        for o in opts:
+            o.reconstruct(fw, 1.0 / PAIRS, SEED, step)
+        total = torch.stack([o.partial for o in opts]).sum(0)
+        for r, o in enumerate(opts):
+            grad = total[r * size:(r + 1) * size]
+            for opt in o.optimizers:
+                opt.step(grad)
+        w.pack()
+    return w, opts, total
+
+
+def _dense_grad(fw, step):
+    from noise_b200 import _lib
+    from noise_b200.model import N_PARAMS
+    g = torch.empty(N_PARAMS, device='cuda')
+    dummy = torch.zeros(1, device='cuda')
+    _lib.call('noise_update_sum_fe_adamw', dummy.data_ptr(), None, None, None, fw.data_ptr(), PAIRS, 1.0 / PAIRS,
+              SEED, step, None, 0.0, 0.0, 0.0, 0.0, 0.0, 0, g.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    return g
+
+
+@pytest.mark.parametrize('world', [2, 8])
+def test_partials_sum_to_the_gradient(world):
+    from noise_b200.shard import ShardPlan
+    w, opts, total = _emulate(world, 'adamw', steps=1)
+    plan = ShardPlan(world)
+    flat = torch.cat([total[r * plan.size:r * plan.size + plan.count[r]] for r in range(world)])
+    want = _dense_grad(_weights(1), 1)
+    torch.testing.assert_close(flat, want, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize('world', [2, 8])
+def test_sharded_adamw_matches_replicated(world):
+    from noise_b200.eggroll import AdamW
+    from noise_b200.model import Weights
+    w, _, _ = _emulate(world, 'adamw')
+    ref = Weights('cuda', seed=0)
+    init = ref.flat.clone()
+    opt = AdamW(ref, lr=1e-3, betas=(0.5, 0.95))
+    for step in (1, 2):
+        opt.set_sum_fe(_weights(step), 1.0 / PAIRS, SEED, step)
+        opt.step()
+    rel, cos = _rel(w.flat - init, ref.flat - init)
+    print('adamw world', world, 'rel', rel, 'cos', cos)
+    assert rel <= 1e-5
+    assert torch.equal(w.packed, ref.packed) or _rel(w.packed.float(), ref.packed.float())[0] < 1e-5
+
+
+@pytest.mark.parametrize('world', [2, 8])
+def test_sharded_anvil_matches_whole_buffer(world):
+    from noise_b200.model import Weights
+    from noise_b200.optim import AdamWDense, Anvil, DenseGrad
+    w, _, _ = _emulate(world, 'anvil')
+    ref = Weights('cuda', seed=0)
+    init = ref.flat.clone()
+    anvil = Anvil(ref, 0.02, 0.01, 100)
+    adam = AdamWDense(ref, 1e-3, (0.5, 0.95))
+    for step in (1, 2):
+        g = DenseGrad(ref)
+        g.flat.copy_(_dense_grad(_weights(step), step))
+        anvil.step(g)
+        adam.step(g)
+    rel, cos = _rel(w.flat - init, ref.flat - init)
+    print('anvil world', world, 'rel', rel, 'cos', cos)
+    assert rel <= 2e-3 and cos >= 0.99999
