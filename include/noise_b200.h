@@ -142,6 +142,16 @@ int noise_dust_errors(const float* clean, const float* perturbed, int draws, int
 int noise_coordinate_differences(const float* raw, const int32_t* targets, int64_t rows, float sigma, float* out,
                                  void* stream);
 
+/* Replaces DUST.reassemble (train/val/run.py:465-471) for a linear site: g[o][i] = sum over the K
+ * tokens of err[k][o] * x[k][i] (err fp32 [K][err_ld], x fp32 or bf16 [K][x_ld], g fp32 [out][in]),
+ * with x's rows first scaled by 1 / rms(x[k][0 .. x_ld)) when x_norm (the normalised module inputs of
+ * mlp.c_fc, lm_head and the attention projections; `in` may be narrower than x_ld, as for ve_gate's
+ * first 32 channels). out % 128 == 0, in % 256 == 0 and K % 32 == 0 run on tf32 tensor cores (the
+ * reference's float32 einsum under 'high' matmul precision); other shapes in fp32 on CUDA cores. */
+int64_t noise_reassemble_workspace_bytes(int K, int out, int in);
+int noise_reassemble(const float* err, int err_ld, int K, int out, const void* x, int x_bf16, int x_ld, int in,
+                     int x_norm, float* g, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* DUST's attention-internal errors (replaces DUST.local_errors, train/val/run.py:391-463). One block,
  * one kind: 0 q, 1 k, 2 v, 3 gate, 4 value embedding (3 and 4 on blocks 1, 3, 5, 7 only). All
  * [B*T, 512] operands are bf16 rows of B sequences of T tokens (T % 128 == 0), 16-byte aligned. */

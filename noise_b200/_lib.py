@@ -41,6 +41,9 @@ SIGNATURES: dict[str, tuple] = {
     'noise_dust_errors': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64, c_uint32, c_int, c_float,
                                   c_float, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
     'noise_coordinate_differences': (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p, c_void_p]),
+    'noise_reassemble_workspace_bytes': (c_int64, [c_int, c_int, c_int]),
+    'noise_reassemble': (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                 c_void_p, c_size_t, c_void_p, c_void_p]),
     'noise_local_process': (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     'noise_local_baseline': (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     'noise_local_workspace_bytes': (c_int64, [c_int, c_int, c_int]),

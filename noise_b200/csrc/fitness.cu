@@ -109,7 +109,7 @@ extern "C" int noise_fitness(const float* losses, int members, int pairs, int mo
   double* f = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(workspace) +
                                         ((size_t)members * sizeof(int32_t) + 255) / 256 * 256);
   const int blocks = (members + 255) / 256;
-  LaunchScope scope(kKindFitness, s);
+  LaunchScope scope(kKindFitness, s, (mode == 1 || ranks) ? 3 : 2);
   if (mode == 1 || ranks) rank_kernel<<<blocks, 256, 0, s>>>(losses, members, rk);
   pair_diff_kernel<<<blocks, 256, 0, s>>>(losses, rk, members, mode, f);
   fold_kernel<<<1, 1024, 0, s>>>(f, members / 2, pairs, mode, weights);

@@ -71,7 +71,7 @@ extern "C" int noise_fitness_static(const float* losses, int members, int pairs,
   int32_t* rk = reinterpret_cast<int32_t*>(scratch);
   double* f = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(scratch) + kStaticRankBytes);
   const int blocks = (members + 255) / 256;
-  LaunchScope scope(kKindFitness, s);
+  LaunchScope scope(kKindFitness, s, (mode == 1 || ranks) ? 3 : 2);
   if (mode == 1 || ranks) rank_kernel<<<blocks, 256, 0, s>>>(losses, members, rk);
   pair_diff_kernel<<<blocks, 256, 0, s>>>(losses, rk, members, mode, f);
   fold_kernel<<<1, 1024, 0, s>>>(f, members / 2, pairs, mode, weights);

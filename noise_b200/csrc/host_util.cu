@@ -80,8 +80,8 @@ static cudaEvent_t pool_event() {
   return g_prof.pool[g_prof.used++];
 }
 
-LaunchScope::LaunchScope(int kind, cudaStream_t s) : kind_(kind), s_(s), idx_(-1) {
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+LaunchScope::LaunchScope(int kind, cudaStream_t s, int kernels) : kind_(kind), s_(s), idx_(-1) {
+  g_launches.fetch_add(kernels, std::memory_order_relaxed);
   std::lock_guard<std::mutex> lk(g_prof.mu);
   if (!g_prof.on) return;
   ProfRecord r{kind, pool_event(), pool_event()};

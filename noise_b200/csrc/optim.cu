@@ -375,7 +375,7 @@ extern "C" int noise_anvil_region_prepare(const NoiseRegion* region, const float
   if (p.count == 0) return kStatusOk;
   p.fast_beta = fast_beta, p.slow_beta = slow_beta, p.beta = beta, p.weight = weight;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  LaunchScope scope(kKindUpdate, s);
+  LaunchScope scope(kKindUpdate, s, 3);
   anvil_blend_kernel<<<p.tiles, kOptBlock, 0, s>>>(p);
   anvil_scalar_kernel<<<1, kMaxMatrices, 0, s>>>(p, 0);
   anvil_cast_kernel<<<p.tiles, kOptBlock, 0, s>>>(p);
@@ -399,7 +399,7 @@ extern "C" int noise_anvil_region_finish(const NoiseRegion* region, float* param
   if (p.count == 0) return kStatusOk;
   p.lane_beta = lane_beta, p.lr = lr, p.wd = weight_decay;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  LaunchScope scope(kKindUpdate, s);
+  LaunchScope scope(kKindUpdate, s, 4);
   anvil_energy_kernel<<<p.lanes, kOptBlock, 0, s>>>(p);
   anvil_norms_kernel<<<p.tiles, kOptBlock, 0, s>>>(p);
   anvil_scalar_kernel<<<1, kMaxMatrices, 0, s>>>(p, 1);

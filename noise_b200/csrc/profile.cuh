@@ -22,9 +22,11 @@ enum LaunchKind : int {
   kNumKinds = 12,
 };
 
+// One scope brackets the launches of one library call; `kernels` is how many kernels it launches
+// (the count noise_launch_count reports), the timing covers them together.
 class LaunchScope {
  public:
-  LaunchScope(int kind, cudaStream_t s);
+  LaunchScope(int kind, cudaStream_t s, int kernels = 1);
   ~LaunchScope();
 
  private:

@@ -84,17 +84,6 @@ class Capture:
         if int(status.item()):
             raise _lib.NoiseError('capture: device wait timed out')
 
-    def module_input(self, s: Site) -> torch.Tensor:
-        """The cached input of the module whose output is jittered (run.py:199, reassemble :467)."""
-        if s.kind == 2:
-            return self.attn_out[s.layer].float()
-        if s.kind == 4:
-            return self.hidden[s.layer].float()
-        if s.kind == 3:
-            m = self.mid[s.layer]
-            return m * torch.rsqrt(m.pow(2).mean(-1, keepdim=True) + torch.finfo(torch.float32).eps)
-        raise ValueError(s.name)
-
 
 def rerun(w: Weights, cap: Capture, sites: list[Site], draws: int, draw_begin: int, sigma: float, entry,
           seed: int, step: int, max_workspace: int = 16 << 30) -> torch.Tensor:
@@ -273,6 +262,29 @@ def head_error(cap: Capture, sigma: float = 0.1) -> torch.Tensor:
     return out.view(cap.B, cap.T, VOCAB)
 
 
+_CONTRACT_WS: dict = {}
+
+
+def contract(err: torch.Tensor, x: torch.Tensor, normalise: bool, width: int | None = None) -> torch.Tensor:
+    """g[o, i] = sum_k err[k, o] x[k, i] (noise_reassemble: tf32 tensor cores), x's rows scaled by
+    1/rms first when `normalise`; `width` keeps x's first columns only (after the row norm)."""
+    err = err.float().contiguous()
+    x = x.contiguous()
+    K, out = err.shape
+    cols = width or x.shape[1]
+    dev = err.device
+    need = int(_lib.load().noise_reassemble_workspace_bytes(K, out, cols))
+    ws = _CONTRACT_WS.get(dev)
+    if ws is None or ws.numel() < need:
+        ws = _CONTRACT_WS[dev] = torch.empty(need, dtype=torch.uint8, device=dev)
+    g = torch.empty(out, cols, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.call('noise_reassemble', err.data_ptr(), out, K, out, x.data_ptr(), int(x.dtype == torch.bfloat16),
+              x.shape[1], cols, int(normalise), g.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
+              _stream(dev))
+    return g
+
+
 def reassemble(cap: Capture, name: str, error: torch.Tensor) -> torch.Tensor:
     """Weight gradient from output error and the cached module input (run.py:465-471)."""
     err = error.reshape(-1, error.shape[-1]).float()
@@ -280,11 +292,15 @@ def reassemble(cap: Capture, name: str, error: torch.Tensor) -> torch.Tensor:
         g = torch.zeros(VOCAB, err.shape[1], dtype=torch.float32, device=err.device)
         return g.index_add_(0, cap.x.reshape(-1).long(), err)
     if name == 'lm_head':
-        fin = cap.final
-        inp = fin * torch.rsqrt(fin.pow(2).mean(-1, keepdim=True) + torch.finfo(torch.float32).eps)
-    else:
-        inp = cap.module_input(site(name))
-    return err.t() @ inp
+        return contract(err, cap.final, True)
+    s = site(name)
+    if s.kind == 2:  # attn.c_proj reads the attention output (bf16)
+        return contract(err, cap.attn_out[s.layer], False)
+    if s.kind == 4:  # mlp.c_proj reads the relu^2 hidden (bf16)
+        return contract(err, cap.hidden[s.layer], False)
+    if s.kind == 3:  # mlp.c_fc reads the normalised stream after the attention
+        return contract(err, cap.mid[s.layer], True)
+    raise ValueError(name)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -399,8 +415,8 @@ def reassemble_local(w: Weights, cap: Capture, kind: str, layer: int, error: tor
     if kind == 've':
         g = torch.zeros(VOCAB, WIDTH, dtype=torch.float32, device=err.device)
         return g.index_add_(0, cap.x.reshape(-1).long(), err)
-    li = inputs or LocalInputs(w, cap, layer)
-    return err.t() @ li.input_of(kind)
+    # the site's input is the normalised block input (its first 32 channels for the gate)
+    return contract(err, cap.blocks[layer], True, 32 if kind == 'gate' else None)
 
 
 # ------------------------------------------------------------------------------------------------
