@@ -221,6 +221,16 @@ int noise_anvil_prepare(const float* grad, float* fast, float* slow, float* scra
 int noise_anvil_finish(float* params, void* packed, const float* slow, const void* update, float* energy,
                        float* partials, float* scalars, float lane_beta, float lr, float weight_decay, void* stream);
 
+/* ANVIL II's `polar` (train/val/run.py:572-580) on the block matrices of a region, in place on x (the
+ * bf16 region buffer noise_anvil_region_prepare wrote): nmaps quintic maps, maps[3k .. 3k+2] = (a, b, c)
+ * of map k, X <- a X + (b S + c S S) X with S = X X^T on each matrix's wide form (the transpose of a
+ * tall c_fc), batched by shape on the tcgen05 engine in bf16 storage with fp32 accumulation. The
+ * workspace holds the stacked matrices (noise_anvil_polar_workspace_bytes; 0 for a region without
+ * block matrices). */
+int64_t noise_anvil_polar_workspace_bytes(const NoiseRegion* region);
+int noise_anvil_region_polar(const NoiseRegion* region, void* x, const float* maps, int nmaps, void* workspace,
+                             size_t workspace_bytes, int* status, void* stream);
+
 /* The same three on the block matrices of one region (grad, fast, slow, scratch and x are region
  * buffers; energy, partials and scalars are sized for the region by noise_anvil_region_sizes). */
 int noise_anvil_region_sizes(const NoiseRegion* region, int64_t* tiles, int64_t* lanes, int* matrices);

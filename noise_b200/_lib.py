@@ -68,6 +68,9 @@ SIGNATURES: dict[str, tuple] = {
                                            c_void_p, c_float, c_float, c_float, c_float, c_void_p]),
     'noise_anvil_region_finish': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_float, c_float, c_float, c_void_p]),
+    'noise_anvil_polar_workspace_bytes': (c_int64, [c_void_p]),
+    'noise_anvil_region_polar': (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p,
+                                         c_void_p]),
     'noise_sum_fe_partial': (c_int, [c_void_p, c_int, c_int, c_int, c_float, c_uint32, c_uint32, c_void_p, c_void_p,
                                      c_void_p]),
     'noise_fitness_static_max_members': (c_int, []),

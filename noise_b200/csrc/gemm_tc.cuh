@@ -42,6 +42,10 @@ struct GemmShape {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
   int* status;
+  // Batched (block-diagonal) products, whole-M-tile schedule only: with batch_m_tiles > 0, rows
+  // [b * batch_m_tiles * 128, (b + 1) * batch_m_tiles * 128) of A meet only rows
+  // [b * batch_n_tiles * 256, (b + 1) * batch_n_tiles * 256) of B: batch b's own product.
+  int batch_m_tiles = 0, batch_n_tiles = 0;
 };
 
 // The tiles of one schedule unit (see the header comment).
@@ -53,6 +57,10 @@ struct TileUnit {
       m = u / s.n_tiles;
       n_begin = u % s.n_tiles;
       n_end = n_begin + 1;
+    } else if (s.batch_m_tiles > 0) {
+      m = u;
+      n_begin = (u / s.batch_m_tiles) * s.batch_n_tiles;
+      n_end = n_begin + s.batch_n_tiles;
     } else {
       m = u;
       n_begin = 0;
@@ -288,7 +296,7 @@ int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, i
 template <class Epi, int kStages>
 int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, int ldb,
                    const typename Epi::Params& ep, int* status, cudaStream_t stream, int kind = kKindOther,
-                   int max_ctas = 0) {
+                   int max_ctas = 0, int batch_m = 0, int batch_n = 0) {
   constexpr bool kTf32 = OperandTf32<Epi>::value;
   constexpr int kElem = kTf32 ? 4 : 2;
   using L = GemmLayout<kStages, kElem>;
@@ -300,6 +308,13 @@ int launch_gemm_tc(const void* A, const void* B, int M, int N, int K, int lda, i
   if (make_tmap_2d(&ta, A, dt, kElem, M, K, lda, L::BM, L::BK)) return kStatusBadArgument;
   if (make_tmap_2d(&tb, B, dt, kElem, N, K, ldb, L::BN, L::BK)) return kStatusBadArgument;
   GemmShape shape{M, N, K, M / L::BM, N / L::BN, K / L::BK, status};
+  if (batch_m > 0) {  // batch_m rows of A against batch_n rows of B, batch by batch
+    if (Epi::kInterleaveN || batch_m % L::BM || batch_n % L::BN || M % batch_m || N % batch_n ||
+        M / batch_m != N / batch_n)
+      return kStatusBadArgument;
+    shape.batch_m_tiles = batch_m / L::BM;
+    shape.batch_n_tiles = batch_n / L::BN;
+  }
   const int smem = 1024 + L::kCoreBytes + Epi::kSmemBytes;
   static bool configured = false;  // one instantiation = one kernel
   if (!configured) {

@@ -1,11 +1,11 @@
 """Optimizers for dense gradients: ANVIL II on the block matrices and AdamW elsewhere, the
 `make_optimizer` split of train/val/run.py:629-656, on noise_b200's kernels.
 
-ANVIL's elementwise and reduction passes run in noise_anvil_prepare / noise_anvil_finish, batched
-over all 48 block matrices; its six quintic maps (`polar`, run.py:572-580) run between them as
-batched bf16 matmuls in the reference's operation order. Tall matrices (c_fc, 2048 x 512) are
-orthogonalised through their right Gram matrix, y <- a y + y (b S + (c S) S) with S = y^T y, which
-equals polar applied to the transpose.
+ANVIL's elementwise and reduction passes run in noise_anvil_region_prepare / _finish, batched over
+the block matrices of a region (all 48 by default); its six quintic maps (`polar`, run.py:572-580)
+run between them in noise_anvil_region_polar: each matrix's wide form (a tall c_fc transposed, as
+polar does) through X <- a X + (b S + c S S) X, S = X X^T, as batched tcgen05 GEMMs in bf16 storage
+with fp32 accumulation.
 """
 from __future__ import annotations
 
@@ -133,14 +133,7 @@ class Anvil:
         self.energy = torch.zeros(max(1, lanes.value), dtype=torch.float32, device=dev)
         self.partials = torch.zeros(max(1, 2 * tiles.value), dtype=torch.float32, device=dev)
         self.scalars = torch.zeros(max(1, mats.value), dtype=torch.float32, device=dev)
-        # views of x per matrix of the region, grouped by shape for batched maps
-        self.wide, self.tall, off = {}, {}, 0
-        for tid, (nm, sh) in enumerate(PARAM_SPECS):
-            k = math.prod(sh)
-            if self.region.tensor_begin <= tid < self.region.tensor_end and is_anvil_matrix(nm, sh):
-                lo = off - self.region.base
-                (self.tall if sh[0] > sh[1] else self.wide).setdefault(sh, []).append(self.x[lo:lo + k].view(sh))
-            off += k
+        self._polar_ws = None
 
     def rail_beta(self):
         lo, hi, cool = self.beta_min, self.beta_max, self.total - self.cooldown
@@ -151,18 +144,13 @@ class Anvil:
         return hi
 
     def _polar_maps(self):
-        for group, tall in ((self.wide, False), (self.tall, True)):
-            for views in group.values():
-                x = torch.stack(views)
-                for a, b, c in MAPS:
-                    if tall:
-                        s = x.transpose(-1, -2) @ x
-                        x = a * x + x @ (b * s + c * s @ s)
-                    else:
-                        s = x @ x.transpose(-1, -2)
-                        x = a * x + (b * s + c * s @ s) @ x
-                for v, xi in zip(views, x):
-                    v.copy_(xi)
+        dev = self.w.device
+        if self._polar_ws is None:
+            n = int(_lib.load().noise_anvil_polar_workspace_bytes(ctypes.byref(self.region)))
+            self._polar_ws = torch.empty(max(1, n), dtype=torch.uint8, device=dev)
+            self._maps = torch.tensor([v for m in MAPS for v in m], dtype=torch.float32)
+        _lib.call('noise_anvil_region_polar', ctypes.byref(self.region), self.x.data_ptr(), self._maps.data_ptr(),
+                  len(MAPS), self._polar_ws.data_ptr(), self._polar_ws.numel(), None, _stream(dev))
 
     @torch.no_grad()
     def step(self, grad):
