@@ -30,6 +30,14 @@ extern "C" {
 int noise_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, float alpha, int out_bf16,
                     int* status, void* stream);
 
+/* Failure-path self-test, no reference counterpart: one launch of the GEMM engine whose producer
+ * arms its operand barrier without issuing the copies, with a wait budget of 2e7 cycles (about
+ * 10 ms). The MMA warp's bounded wait runs out, the kernel sets *status = NOISE_WAIT_TIMEOUT and ends
+ * through its abort path (every role leaves its loop, tensor memory is freed); the context stays
+ * usable. A: bf16 [128][64], B: bf16 [256][64] device buffers (never read); returns NOISE_OK when the
+ * launch succeeded. */
+int noise_selftest_wait_timeout(const void* A, const void* B, int* status, void* stream);
+
 /* Number of fp32 master parameters (37,749,776): one flat buffer in `GPT.named_parameters()` order
  * (utils/model.py:123-147), which is also the `final.pt` state-dict order and the draw-stream tensor
  * id order. */

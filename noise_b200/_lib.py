@@ -25,6 +25,7 @@ c_void_p, c_int, c_float, c_int64, c_uint32, c_size_t, c_uint64 = (
 SIGNATURES: dict[str, tuple] = {
     'noise_gemm_bf16': (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int,
                                 c_void_p, c_void_p]),
+    'noise_selftest_wait_timeout': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     'noise_param_count': (c_int64, []),
     'noise_packed_count': (c_int64, []),
     'noise_pack_weights': (c_int, [c_void_p, c_void_p, c_void_p]),

@@ -39,7 +39,31 @@ struct EpiStore {
   }
 };
 
+// The engine's failure path, exercised without a fault: the producer arms the operand barrier but
+// issues no copy, so the MMA warp's wait for the first stage runs out after kWaitBudget cycles
+// (about 10 ms), sets the abort flag and the status word, and every role leaves its loop, drains and
+// frees tensor memory. Nothing is stored.
+struct EpiWaitTimeout {
+  struct Params {};
+  static constexpr int kSmemBytes = 0;
+  static constexpr bool kInterleaveN = false;
+  static constexpr bool kSkipLoads = true;
+  static constexpr long long kWaitBudget = 20ll * 1000 * 1000;
+  __device__ EpiWaitTimeout(const Params&, uint8_t*, int, int) {}
+  __device__ void begin_mtile(int, int) {}
+  __device__ void begin_tile(int, int, int) {}
+  __device__ void end_mtile(int, int, int) {}
+  __device__ void group(int, int, float (&)[64]) {}
+};
+
 }  // namespace noise
+
+extern "C" int noise_selftest_wait_timeout(const void* A, const void* B, int* status, void* stream) {
+  if (!A || !B || !status) return noise::kStatusBadArgument;
+  noise::EpiWaitTimeout::Params ep{};
+  return noise::launch_gemm_tc<noise::EpiWaitTimeout, 3>(A, B, 128, 256, 64, 64, 64, ep, status,
+                                                          reinterpret_cast<cudaStream_t>(stream));
+}
 
 extern "C" int noise_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                                int out_bf16, int* status, void* stream) {

@@ -80,6 +80,19 @@ struct OperandTf32 : std::false_type {};
 template <class E>
 struct OperandTf32<E, std::void_t<decltype(E::kTf32)>> : std::integral_constant<bool, E::kTf32> {};
 
+// Self-test traits (the wait-timeout test instantiation): kWaitBudget replaces the cycle budget of
+// every wait; kSkipLoads makes the producer arm its barriers without issuing the copies, so the MMA
+// warp's first wait runs out and the kernel ends through its timeout path.
+template <class E, class = void>
+struct WaitBudget : std::integral_constant<long long, kWaitCycleBudget> {};
+template <class E>
+struct WaitBudget<E, std::void_t<decltype(E::kWaitBudget)>> : std::integral_constant<long long, E::kWaitBudget> {};
+
+template <class E, class = void>
+struct SkipsLoads : std::false_type {};
+template <class E>
+struct SkipsLoads<E, std::void_t<decltype(E::kSkipLoads)>> : std::integral_constant<bool, E::kSkipLoads> {};
+
 template <class E, class = void>
 struct HasFinish : std::false_type {};
 template <class E>
@@ -104,6 +117,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmShape shape, const __grid_constant__ typename Epi::Params ep) {
   constexpr bool kTf32 = OperandTf32<Epi>::value;
+  constexpr long long kBudget = WaitBudget<Epi>::value;
   using L = GemmLayout<kStages, kTf32 ? 4 : 2>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,11 +175,15 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
         const int m = tu.m;
         for (int n = tu.n_begin; ok && n < tu.n_end; ++n) {
           for (int kb = 0; kb < shape.k_blocks; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status)) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kBudget)) {
               ok = false;
               break;
             }
             mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+            if constexpr (SkipsLoads<Epi>::value) {
+              if (++stage == kStages) stage = 0, phase ^= 1;
+              continue;  // self-test: the barrier waits for bytes that never come
+            }
             tma_load_2d(sA + stage * L::kABytes, &tmA, &full[stage], kb * L::BK, m * L::BM);
             tma_load_2d_hint(sB + stage * L::kBBytes, &tmB, &full[stage], kb * L::BK, n * L::BN, keep);
             issued[stage] = true;
@@ -176,7 +194,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       }
       // Every copy this thread started lands before the CTA can exit.
       for (int s = 0; s < kStages; ++s)
-        if (issued[s]) mbar_wait(&full[s], issued_phase[s], abort_flag, status);
+        if (issued[s]) mbar_wait(&full[s], issued_phase[s], abort_flag, status, kBudget);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -189,14 +207,14 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
         const TileUnit<Epi::kInterleaveN> tu(u, shape);
         for (int n = tu.n_begin; ok && n < tu.n_end; ++n, ++t) {
           const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;
-          if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status)) {
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status, kBudget)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t d = tmem_base + acc * L::BN;
           for (int kb = 0; kb < shape.k_blocks; ++kb) {
-            if (!mbar_wait(&full[stage], phase, abort_flag, status)) {
+            if (!mbar_wait(&full[stage], phase, abort_flag, status, kBudget)) {
               ok = false;
               break;
             }
@@ -216,7 +234,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       }
       // No MMA may still be writing TMEM when it is freed.
       tc_commit(drain);
-      mbar_wait(drain, 0, abort_flag, status);
+      mbar_wait(drain, 0, abort_flag, status, kBudget);
     }
     __syncwarp();
   } else {
@@ -244,7 +262,7 @@ __global__ void __launch_bounds__(GemmLayout<kStages>::kThreads, 1)
       epi.begin_mtile(m, row);
       for (int n = tu.n_begin; n < tu.n_end; ++n, ++t) {
         const uint32_t acc = t & 1, acc_phase = (t >> 1) & 1;
-        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status)) {
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status, kBudget)) {
           ok = false;
           break;
         }

@@ -82,15 +82,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Bounded wait on a phase parity. Returns false when the cycle budget ran out or when another role
 // of the same CTA raised `abort` (a shared flag); in the first case the global status is set.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* status) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                          long long budget = kWaitCycleBudget) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if ((it & 15u) == 0) {
       if (*abort) return false;
-      if (clock64() - start > kWaitCycleBudget) {
+      if (clock64() - start > budget) {
         *abort = 1;
         if (status) atomicExch(status, kStatusWaitTimeout);
         return false;
