@@ -2,7 +2,8 @@
 
 - the head's gradient equals reassemble(head_error) / valid tokens, exactly (same kernels);
 - the mixing scalars' two-sided ES estimate against the same ES run through the CPU oracle's fp32
-  forward with the same directions (bf16 GEMM operands: cosine >= 0.98, relative L2 <= 0.2);
+  forward with the same directions: cosine >= 0.999 and relative L2 <= 0.05 (bf16 GEMM operands in
+  the blocks and the fp32 head on tf32 MMAs, against fp32; measured cosine 0.99993, relative 0.013);
 - the step leaves the weights as they were when the optimizer does nothing, and every estimate is
   finite; the returned loss is the clean mean loss of the oracle's forward (rel 2e-3).
 """
@@ -79,7 +80,7 @@ def test_dust_step_pieces():
     rel = ((got - est_o).norm() / est_o.norm()).item()
     cos = torch.nn.functional.cosine_similarity(got, est_o, dim=0).item()
     print('scalar ES rel', rel, 'cos', cos)
-    assert cos >= 0.98 and rel <= 0.2, (rel, cos)
+    assert cos >= 0.999 and rel <= 0.05, (rel, cos)
 
 
 def test_dust_step_with_optimizers_lowers_loss():
