@@ -532,7 +532,7 @@ def run_dust(args, rank, world, local):
 # DRAM bytes (read + write) per population row of one launch of each kind, from one ncu capture of the
 # small case (262,144 rows per launch); traffic grows in proportion to the rows, so a bench launch's
 # traffic is this times its rows.
-TRAFFIC_BYTES_PER_ROW = {'attention': 4063, 'qkv': 4246, 'proj': 6214, 'fc': 5057, 'mlp': 9743}
+TRAFFIC_BYTES_PER_ROW = {'attention': 4063, 'qkv': 4523, 'proj': 6203, 'fc': 5071, 'mlp': 9548}
 
 
 def ctypes_array(code, n):
