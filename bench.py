@@ -341,7 +341,9 @@ def main():
 
     extras = {}
     if not args.no_extras:
-        extras['fixed_population'] = fixed_population(rank, world, dev, FIXED_MEMBERS, args.sigma, barrier)
+        # one timed update where an update takes tens of seconds (up to 2 GPUs), two above
+        extras['fixed_population'] = fixed_population(rank, world, dev, FIXED_MEMBERS, args.sigma, barrier,
+                                                      steps=1 if world <= 2 else 2)
         extras['dust'] = {f'{scale}': dust_update(rank, world, dev, scale, steps, barrier)
                           for scale, steps in DUST_SCALES}
         if world >= 8:
