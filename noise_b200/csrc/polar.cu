@@ -187,11 +187,11 @@ PolarGroups polar_groups(const NoiseRegion& region, void* x, void* ws) {
     PolarCopy& c = G.g[big == kPolarR ? 0 : 1];
     c.item[c.count++] = PolarItem{L.offset[tid] - region.base, L.rows[tid], L.cols[tid]};
   }
-  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
   size_t off = 0;
   for (PolarCopy& c : G.g) {
     c.region = reinterpret_cast<__nv_bfloat16*>(x);
-    c.X = reinterpret_cast<__nv_bfloat16*>(p + off);  // X[0], X[1], XT[0], XT[1], S, Bm follow
+    // X[0], X[1], XT[0], XT[1], S, Bm follow; a size query (no workspace) carves nothing
+    c.X = ws ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ws) + off) : nullptr;
     off += polar_group_bytes(c.count, c.R, c.C);
   }
   G.bytes = off;
