@@ -445,18 +445,19 @@ def dust_update(rank, world, dev, scale, steps, barrier, warmup=1):
     from noise_b200.data import zipf_tokens
     from noise_b200.dust import DUST, recipe
     from noise_b200.model import Weights
-    from noise_b200.optim import make_optimizer
+    from noise_b200.optim import make_sharded_optimizer
     rec = recipe(scale)
     w = Weights(dev, seed=0)
     est = DUST(w, rec, 0, rank, world)
-    opt = make_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 610)
+    opt = make_sharded_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 610, rank, world)
     rows = zipf_tokens(BATCH, SEQ + 1, seed=1).pin_memory()
     x, y = rows[:, :-1], rows[:, 1:]
     ms = timed_steps(lambda: est.step(x, y, opt), steps, warmup, barrier, dev)
     draws = sum(rec.writers) + sum(rec.hidden) + sum(rec.hubs) + rec.embedding + sum(rec.local.values())
     published = DUST_PUBLISHED_8XH100.get(scale)
     return {'recipe_scale': scale, 'draws_per_update': draws, 's_per_update': ms / 1e3, 'steps': steps,
-            'warmup': warmup, 'reference_8xh100_s_per_update': published, 'scaling': 'strong'}
+            'warmup': warmup, 'reference_8xh100_s_per_update': published, 'scaling': 'strong',
+            'update': 'estimate reduce-scattered, ANVIL II / AdamW on owned tensors, parameter all-gather'}
 
 
 # The reference's own logs on 8xH100 (train/val/log, train/speedrun/log): seconds per DUST update.

@@ -565,6 +565,12 @@ class DUST:
         self.memory.calibrate()  # the next step's alpha
         valid = (cap.y >= 0).sum().float()
         grads.flat.div_(valid)
+        if hasattr(optimizer, 'step_dense'):
+            # sharded update: the ranks' shares are reduce-scattered, not all-reduced
+            if not optimizer.step_dense(grads.flat, 1.0 / self.world):
+                raise FloatingPointError('Non-finite estimate')
+            self.memory.remember(self.credit, valid)
+            return cap.clean_loss.view(cap.B, cap.T)[cap.y >= 0].mean().item()
         self._average(grads.flat)
         if not torch.isfinite(grads.flat).all():
             raise FloatingPointError('Non-finite estimate')

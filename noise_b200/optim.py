@@ -191,3 +191,12 @@ class Optimizers:
 def make_optimizer(w: Weights, lr: float, betas, anvil_lr: float, anvil_wd: float, steps: int) -> Optimizers:
     """ANVIL II on block matrices, AdamW elsewhere (run.py:643-656)."""
     return Optimizers(Anvil(w, anvil_lr, anvil_wd, steps), AdamWDense(w, lr, betas, eps=1e-8, weight_decay=0.0))
+
+
+def make_sharded_optimizer(w: Weights, lr: float, betas, anvil_lr: float, anvil_wd: float, steps: int, rank: int = 0,
+                           world: int = 1):
+    """The same split on the sharded update (noise_b200.shard): each rank owns a run of whole tensors,
+    the gradient is reduce-scattered instead of all-reduced, and the parameters are all-gathered."""
+    from .shard import ShardedOptimizer
+    return ShardedOptimizer(w, rank, world, kind='anvil', lr=lr, betas=betas, eps=1e-8, weight_decay=0.0,
+                            anvil_lr=anvil_lr, anvil_wd=anvil_wd, steps=steps)

@@ -169,6 +169,34 @@ class ShardedOptimizer:
             opt.step(self.grad)
         self.exchange_parameters()
 
+    @torch.no_grad()
+    def step_dense(self, flat: torch.Tensor, scale: float = 1.0) -> bool:
+        """One update from this rank's share of a dense gradient in the flat layout (DUST's estimate,
+        whose draws are split over the ranks): the shares are summed by the reduce-scatter, times
+        `scale` (1 / world for the reference's average, train/val/run.py:511-515), each rank steps its
+        region and the all-gather restores the model. The reference checks the averaged gradient for
+        non-finite values before stepping (:528-529); here every rank checks its summed region and the
+        verdict is all-reduced, so all ranks skip together. Returns False (nothing stepped) on a
+        non-finite gradient."""
+        plan = self.plan
+        for r in range(self.world):
+            if plan.count[r]:
+                self.partial[r * plan.size:r * plan.size + plan.count[r]].copy_(
+                    flat[plan.begin[r]:plan.begin[r] + plan.count[r]])
+        self.exchange_gradients()
+        n = plan.count[self.rank]
+        if scale != 1.0:
+            self.grad[:n].mul_(scale)
+        bad = (~torch.isfinite(self.grad[:n])).any().to(torch.float32).reshape(1)
+        if self.world > 1:
+            torch.distributed.all_reduce(bad)
+        if bad.item():
+            return False
+        for opt in self.optimizers:
+            opt.step(self.grad)
+        self.exchange_parameters()
+        return True
+
     def reconstruct(self, fw: torch.Tensor, scale: float, seed: int, step: int):
         """This rank's directions, contracted into the padded layout of every tensor."""
         pairs = fw.numel()

@@ -102,3 +102,26 @@ def test_dust_step_with_optimizers_lowers_loss():
     # the credit memory is written every step and its priors are fitted after the second
     assert est.memory.P is not None and len(est.memory.S) == 8 * 3 + 1 + 8
     assert set(est.memory.alpha) == set(est.memory.S)
+
+
+def test_dust_step_sharded_optimizer_matches_replicated():
+    """One DUST step through the sharded optimizer (its dense-gradient entry) leaves the same weights as
+    the replicated ANVIL II + AdamW (one process: the whole buffer is one region, so the two apply the
+    same kernels to the same gradient: relative L2 of the weight changes <= 1e-6)."""
+    from noise_b200.dust import DUST, LAYERS, Recipe
+    from noise_b200.model import Weights
+    from noise_b200.optim import make_optimizer, make_sharded_optimizer
+    x, y = _batch()
+    rec = Recipe(writers=[32] * LAYERS, hidden=[32] * LAYERS, hubs=[32] * LAYERS, embedding=32,
+                 local=dict(q=16, v=16, gate=16, k=16, ve=16), nrep=16, lr=0.003)
+    out = []
+    for make in (make_optimizer, make_sharded_optimizer):
+        w = Weights('cuda', seed=0)
+        before = w.flat.clone()
+        opt = make(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 100)
+        DUST(w, rec, seed=0).step(x, y, opt)
+        torch.cuda.synchronize()
+        out.append((w.flat - before).double())
+    rel = ((out[1] - out[0]).norm() / out[0].norm()).item()
+    print('sharded vs replicated DUST step: rel', rel)
+    assert out[0].abs().sum() > 0 and rel <= 1e-6

@@ -115,3 +115,51 @@ def test_two_ranks_match_one(tmp_path):
     assert torch.equal(got[0], got[1])
     torch.testing.assert_close(got[0], single, rtol=1e-6, atol=1e-7)
     assert not torch.equal(single, CpuWeights().flat)
+
+
+def _run_dense(rank, world, steps=2):
+    """Each rank holds its own share of a dense gradient (rank-dependent); the update must equal one
+    process stepping with the average of the shares."""
+    from noise_b200.shard import ShardedOptimizer, ShardPlan
+    w = CpuWeights()
+    opt = ShardedOptimizer(w, rank, world, kernels=CpuKernels(),
+                           optimizers=[RegionSgd(w, ShardPlan(world).region(rank))])
+    i = torch.arange(N_PARAMS, dtype=torch.float64)
+    for step in range(1, steps + 1):
+        if world == 1:  # one process: the average of both ranks' shares
+            share = sum(torch.sin(0.3 * step + 0.7 * r + 1e-5 * i) for r in range(2)).float() / 2
+        else:
+            share = torch.sin(0.3 * step + 0.7 * rank + 1e-5 * i).float()
+        assert opt.step_dense(share, 1.0 / world)
+    return w.flat
+
+
+def _worker_dense(rank, world, port, out):
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        torch.save(_run_dense(rank, world), f'{out}.{rank}')
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dense_shares_two_ranks_match_one(tmp_path):
+    """DUST's path: the ranks' dense gradient shares reduce-scattered and averaged, regions stepped,
+    parameters all-gathered (rtol 1e-6 against one process with the averaged gradient)."""
+    single = _run_dense(0, 1)
+    out = str(tmp_path / 'dense')
+    mp.start_processes(_worker_dense, args=(2, _free_port(), out), nprocs=2, start_method='spawn')
+    got = [torch.load(f'{out}.{r}') for r in range(2)]
+    assert torch.equal(got[0], got[1])
+    torch.testing.assert_close(got[0], single, rtol=1e-6, atol=1e-7)
+
+
+def test_dense_step_refuses_non_finite():
+    from noise_b200.shard import ShardedOptimizer, ShardPlan
+    w = CpuWeights()
+    before = w.flat.clone()
+    opt = ShardedOptimizer(w, 0, 1, kernels=CpuKernels(), optimizers=[RegionSgd(w, ShardPlan(1).region(0))])
+    g = torch.zeros(N_PARAMS)
+    g[12345] = float('nan')
+    assert opt.step_dense(g) is False
+    assert torch.equal(w.flat, before)
