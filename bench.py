@@ -472,7 +472,7 @@ def run_dust(args, rank, world, local):
     from noise_b200.data import zipf_tokens
     from noise_b200.dust import DUST, recipe
     from noise_b200.model import Weights
-    from noise_b200.optim import make_optimizer
+    from noise_b200.optim import make_sharded_optimizer
 
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
@@ -482,7 +482,7 @@ def run_dust(args, rank, world, local):
     rec = recipe(args.dust_scale)
     w = Weights(dev, seed=0)
     est = DUST(w, rec, 0, rank, world)
-    opt = make_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 610)
+    opt = make_sharded_optimizer(w, rec.lr, rec.betas, rec.anvil_lr, rec.anvil_wd, 610, rank, world)
     rows = zipf_tokens(BATCH, SEQ + 1, seed=1).pin_memory()
     x, y = rows[:, :-1], rows[:, 1:]
     for _ in range(args.warmup):

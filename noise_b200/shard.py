@@ -173,9 +173,9 @@ class ShardedOptimizer:
     def step_dense(self, flat: torch.Tensor, scale: float = 1.0) -> bool:
         """One update from this rank's share of a dense gradient in the flat layout (DUST's estimate,
         whose draws are split over the ranks): the shares are summed by the reduce-scatter, times
-        `scale` (1 / world for the reference's average, train/val/run.py:511-515), each rank steps its
+        `scale` (1 / world for the reference's average, train/val/run.py:536, average_ranks at :154-158), each rank steps its
         region and the all-gather restores the model. The reference checks the averaged gradient for
-        non-finite values before stepping (:528-529); here every rank checks its summed region and the
+        non-finite values before stepping (:537-538); here every rank checks its summed region and the
         verdict is all-reduced, so all ranks skip together. Returns False (nothing stepped) on a
         non-finite gradient."""
         plan = self.plan
