@@ -3,22 +3,25 @@
 // RMS-normalised per head by the QKV epilogue.
 //
 // One CTA = G consecutive 128-query tiles x one head x one (member, sequence) row block. The G tiles
-// share every K/V tile the CTA streams. The kernel is bound by the hand-offs between its roles, not
-// by the tensor or exp2 units, so it is sized for several independent CTAs per SM: G = 2, 96
-// registers, a 3-stage K ring and a 2-stage V ring (2 CTAs and 20 warps per SM; G = 1 when the tile
-// count is odd). Warps:
+// share every K/V tile the CTA streams. The kernel is bound by the latency of each query tile's
+// S -> softmax -> P -> PV cycle, not by the tensor or exp2 units, so it holds as many query tiles per
+// SM as TMEM allows: G = 2, 96 registers, a 3-stage K ring and a 2-stage V ring (2 CTAs and 20 warps
+// per SM; G = 1 when the tile count is odd). Warps:
 //   warp 0       TMA producer: the G Q tiles once, then 64-key K and V tiles, K two tiles ahead of V
 //   warp 1       TMEM owner and MMA issuer (one thread), per key tile j and query tile g:
-//                  S_g  = Q_g K_j^T    tcgen05.mma M=128 N=64 K=64, A and B K-major
-//                  O_g += P_g V_j      tcgen05.mma M=128 N=64 K=64, A = P_g (K-major smem), B = V (MN-major)
+//                  O_g += P_g V_{j-1}  tcgen05.mma M=128 N=64 K=64, A = P_g from TMEM, B = V (MN-major smem)
+//                  S_g  = Q_g K_j^T    tcgen05.mma M=128 N=64 K=64, A and B K-major smem
 //   warps 2..    softmax group g = 4 warps, one query row per thread: S_g from TMEM -> p = exp(s/8 - 8)
-//                (masked) -> bf16 P_g in a 128-byte-swizzled smem tile; at the end O_g / sum(p) -> y, y.b_proj.
-// The groups run out of phase with each other, so the single MMA thread keeps the tensor core busy
-// while the special-function unit works through the exponentials.
+//                (masked) -> bf16 P_g written back over S_g's first 32 TMEM columns; at the end
+//                O_g / sum(p) -> y, y.b_proj.
+// P never passes through shared memory: the PV product reads it from TMEM, and S_g of the next key
+// tile is issued after that product (the tensor core runs one thread's products in issue order).
+// The groups run out of phase with each other, so the tensor core serves one group's products while
+// the special-function unit works through another's exponentials.
 // Because q and k are unit-RMS, |q.k| / 8 <= 8 (up to bf16 rounding), so the softmax uses the fixed
 // offset 8: no running maximum and no rescaling of the TMEM accumulator. Each query tile walks only
 // the key tiles its window reaches; 32-key chunks outside a warp's rows' windows skip their
-// exponentials. TMEM: group g uses S at 128g and O at 128g + 64.
+// exponentials. TMEM: group g uses S (then P) at 128g and O at 128g + 64.
 // Every wait is bounded (status word on timeout).
 //
 // Score mode (kScore, DUST's attention reruns, train/val/run.py:391-463): Q, K and V each come from
@@ -50,21 +53,17 @@ struct AttnTcParams {
 constexpr int kAtQ = 128;
 constexpr int kAtQBytes = kAtQ * kHeadDim * 2;  // 16 KB
 
-// G query tiles per CTA, key tiles of KT keys (64 or 128). A K or V tile is KT rows x 128 B; P is KT / 64
-// swizzled sub-tiles of 128 rows x 64 keys per query tile. TMEM per query tile: S (KT columns), then O.
+// G query tiles per CTA, key tiles of KT keys (64 or 128). A K or V tile is KT rows x 128 B. TMEM per
+// query tile: S (KT columns, P over its first KT / 2 once S is read), then O.
 // K and V have rings of their own: a K stage is free once the S products have read it, a V stage
 // once the PV products have, and the producer keeps K kKStages - 1 tiles ahead of V.
 template <int G, int KT>
 struct AttnTcLayout {
   static constexpr int kThreads = (2 + 4 * G) * 32;
   static constexpr int kTileBytes = KT * kHeadDim * 2;
-  static constexpr int kPBytes = kAtQ * KT * 2;
   static constexpr int kKStages = KT == 64 ? 3 : 2, kVStages = 2;
-  static constexpr int kCore = G * kAtQBytes + (kKStages + kVStages) * kTileBytes + G * kPBytes;
-  // 128-key tiles fit two CTAs per SM only without the alignment slack: the kernel then checks that
-  // the dynamic shared base is 1024-aligned (it follows the per-CTA reserved kilobyte)
-  static constexpr int kSlack = KT == 64 ? 1024 : 0;
-  static constexpr int kSmem = kSlack + kCore + 512 + kHeadDim * 4;
+  static constexpr int kCore = G * kAtQBytes + (kKStages + kVStages) * kTileBytes;
+  static constexpr int kSmem = 1024 + kCore + 512 + kHeadDim * 4;  // 1 KB for the 1024-byte alignment
   static constexpr uint32_t kGroupCols = KT == 64 ? 128 : 256;
   static constexpr uint32_t kTmemCols = kGroupCols * G;
 };
@@ -75,15 +74,13 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ AttnTcParams p) {
   using L = AttnTcLayout<G, KT>;
-  constexpr int kAtK = KT, kAtTileBytes = L::kTileBytes, kAtPBytes = L::kPBytes;
+  constexpr int kAtK = KT, kAtTileBytes = L::kTileBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const bool misaligned = L::kSlack == 0 && base != smem_raw;
   uint8_t* sQ = base;                              // [g] 16 KB
   constexpr int KS = L::kKStages, VS = L::kVStages;
   uint8_t* sK = sQ + G * kAtQBytes;         // [stage] KT x 128 B
   uint8_t* sV = sK + KS * kAtTileBytes;     // [stage] KT x 128 B
-  uint8_t* sP = sV + VS * kAtTileBytes;     // [g] KT / 64 sub-tiles of 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kCore);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;      // [KS]
@@ -91,10 +88,8 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
   uint64_t* v_full = k_empty + KS;    // [VS]
   uint64_t* v_empty = v_full + VS;    // [VS]
   uint64_t* s_full = v_empty + VS;    // [G]
-  uint64_t* s_empty = s_full + G;            // [G]
-  uint64_t* p_full = s_empty + G;            // [G]
-  uint64_t* p_empty = p_full + G;            // [G]
-  uint64_t* o_full = p_empty + G;
+  uint64_t* p_full = s_full + G;      // [G]
+  uint64_t* o_full = p_full + G;
   uint64_t* drain = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -110,7 +105,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
   const int q0 = unit * kAtQ * G;  // first query of the CTA
   const int kt_begin = max(0, q0 - p.window) / kAtK;
   const int kt_end = (q0 + kAtQ * G - 1) / kAtK;
-  const int n_kt = misaligned ? 0 : kt_end - kt_begin + 1;
+  const int n_kt = kt_end - kt_begin + 1;
   // Each query tile g needs only key tiles [g_lo(g), g_hi(g)] of the CTA's range (relative indices):
   // the tiles before its window are skipped by the MMA and softmax roles alike.
   auto g_lo = [&](int g) { return max(0, q0 + kAtQ * g - p.window) / kAtK - kt_begin; };
@@ -123,14 +118,11 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
     for (int s = 0; s < VS; ++s) mbar_init(&v_full[s], 1), mbar_init(&v_empty[s], 1);
     for (int g = 0; g < G; ++g) {
       mbar_init(&s_full[g], 1);
-      mbar_init(&s_empty[g], 4);
       mbar_init(&p_full[g], 4);
-      mbar_init(&p_empty[g], 1);
     }
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
-    *abort_flag = misaligned ? 1 : 0;
-    if (misaligned) atomicExch(p.status, kStatusUnsupported);
+    *abort_flag = 0;
     fence_mbarrier_init();
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
@@ -156,11 +148,9 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       const int64_t rq = operand_rows(p.mod_q), rk = operand_rows(p.mod_k), rv = operand_rows(p.mod_v);
-      if (!misaligned) {
-        mbar_arrive_expect_tx(q_full, G * kAtQBytes);
-        for (int b = 0; b < 2 * G; ++b)
-          tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_q, q_full, qcol, (int)(rq + q0 + 64 * b));
-      }
+      mbar_arrive_expect_tx(q_full, G * kAtQBytes);
+      for (int b = 0; b < 2 * G; ++b)
+        tma_load_2d(sQ + b * (kAtQBytes / 2), &tm_q, q_full, qcol, (int)(rq + q0 + 64 * b));
       // order K(0) .. K(KS - 2), then K(j + KS - 1) before V(j): each wait is for a stage that the
       // products issued before the one the next copy feeds have released
       int nk = 0, nv = 0;
@@ -181,67 +171,61 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
         else ok = load(false, nv++);
       }
       // copies in flight land before the CTA can exit
-      if (!misaligned) mbar_wait(q_full, 0, abort_flag, status);
+      mbar_wait(q_full, 0, abort_flag, status);
       for (int j = max(0, nk - KS); j < nk; ++j) mbar_wait(&k_full[j % KS], (j / KS) & 1, abort_flag, status);
       for (int j = max(0, nv - VS); j < nv; ++j) mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
+      // Per key tile j, for each query tile g: PV(j - 1), then S(j). P(j - 1) lies in the TMEM columns
+      // of S(j - 1), so S(j) is issued only after the PV product that reads them (the tensor core
+      // runs one thread's products in issue order).
       const uint32_t idesc_s = make_idesc(1, kAtQ, kAtK);
       const uint32_t idesc_o = make_idesc(1, kAtQ, kHeadDim, 0, 1);  // B = V is MN-major
       bool ok = mbar_wait(q_full, 0, abort_flag, status);
       tc_fence_after();
       for (int j = 0; ok && j <= n_kt; ++j) {
-        if (j < n_kt) {
-          const int st = j % KS;
-          if (!mbar_wait(&k_full[st], (j / KS) & 1, abort_flag, status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t dk = smem_desc_sw128(sK + st * kAtTileBytes);
-          for (int g = 0; g < G && ok; ++g) {
-            if (j < g_lo(g) || j > g_hi(g)) continue;
-            if (!mbar_wait(&s_empty[g], ((j - g_lo(g)) & 1) ^ 1, abort_flag, status)) {
+        const int jj = j - 1;
+        bool v_ready = false, k_ready = false;
+        for (int g = 0; g < G && ok; ++g) {
+          const int lo = g_lo(g), hi = g_hi(g);
+          const uint32_t tG = tmem + L::kGroupCols * g;  // S, then P over its first columns
+          if (jj >= lo && jj <= hi) {
+            if (!v_ready && !(v_ready = mbar_wait(&v_full[jj % VS], (jj / VS) & 1, abort_flag, status))) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint64_t dq = smem_desc_sw128(sQ + g * kAtQBytes);
-#pragma unroll
-            for (int k = 0; k < kHeadDim / 16; ++k)
-              tc_mma_f16(tmem + L::kGroupCols * g, dq + 2 * k, dk + 2 * k, idesc_s, k > 0 ? 1u : 0u);
-            tc_commit(&s_full[g]);
-          }
-          if (ok) tc_commit(&k_empty[st]);
-        }
-        if (ok && j > 0) {
-          const int jj = j - 1, st = jj % VS;
-          if (!mbar_wait(&v_full[st], (jj / VS) & 1, abort_flag, status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t dv = smem_desc_sw128_mn(sV + st * kAtTileBytes);
-          for (int g = 0; g < G && ok; ++g) {
-            const int lo = g_lo(g);
-            if (jj < lo || jj > g_hi(g)) continue;
             if (!mbar_wait(&p_full[g], (jj - lo) & 1, abort_flag, status)) {
               ok = false;
               break;
             }
             tc_fence_after();
+            const uint64_t dv = smem_desc_sw128_mn(sV + (jj % VS) * kAtTileBytes);
 #pragma unroll
-            for (int k = 0; k < kAtK / 16; ++k) {
-              const uint64_t dp = smem_desc_sw128(sP + g * kAtPBytes + (k >> 2) * 16384);
-              tc_mma_f16(tmem + L::kGroupCols * g + KT, dp + 2 * (k & 3), dv + (uint64_t)(2048 >> 4) * k, idesc_o,
-                         (jj > lo || k > 0) ? 1u : 0u);
-            }
-            tc_commit(&p_empty[g]);
+            for (int k = 0; k < kAtK / 16; ++k)  // 16 keys of P = 8 TMEM columns
+              tc_mma_f16_ts(tG + KT, tG + 8 * k, dv + (uint64_t)(2048 >> 4) * k, idesc_o, (jj > lo || k > 0) ? 1u : 0u);
           }
-          if (ok) tc_commit(&v_empty[st]);
+          if (j < n_kt && j >= lo && j <= hi) {
+            if (!k_ready) {
+              if (!(k_ready = mbar_wait(&k_full[j % KS], (j / KS) & 1, abort_flag, status))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint64_t dk = smem_desc_sw128(sK + (j % KS) * kAtTileBytes);
+            const uint64_t dq = smem_desc_sw128(sQ + g * kAtQBytes);
+#pragma unroll
+            for (int k = 0; k < kHeadDim / 16; ++k)
+              tc_mma_f16(tG, dq + 2 * k, dk + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+            tc_commit(&s_full[g]);
+          }
         }
+        if (!ok) break;
+        // every tile of [0, n_kt) is used by at least one query tile
+        if (jj >= 0) tc_commit(&v_empty[jj % VS]);
+        if (j < n_kt) tc_commit(&k_empty[j % KS]);
       }
       if (ok) tc_commit(o_full);
       tc_commit(drain);
@@ -263,7 +247,6 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
     const float2 kScale2 = make_float2(kScaleLog2, kScaleLog2), kNegOffset2 = make_float2(-kOffsetLog2, -kOffsetLog2);
     float2 lsum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     bool ok = true;
-    uint8_t* prow = sP + g * kAtPBytes + r * 128;
     const int qlo = qg + quarter * 32, qhi = qlo + 31;  // this warp's rows
     const int j_lo = g_lo(g), j_hi = g_hi(g);
     for (int j = j_lo; j <= j_hi; ++j) {
@@ -275,68 +258,50 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int h = 0; h < KT / 64; ++h) {  // 64-key halves of S, each into its own P sub-tile
-      float sv[64];
-      tmem_ld64(tS + lane_addr + 64 * h, sv);
-      if (h == KT / 64 - 1) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[g]);
-      }
-      if (h == 0 && !mbar_wait(&p_empty[g], par ^ 1, abort_flag, status)) {
-        ok = false;
-        break;
-      }
-      uint8_t* ph = prow + h * 16384;
+      for (int h = 0; h < KT / 64; ++h) {  // 64-key parts of S; P (bf16 pairs) goes over S's first columns
+        {
+          float sv[64];
+          tmem_ld64(tS + lane_addr + 64 * h, sv);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int kc = k0 + 64 * h + 32 * c;
-        // warp-uniform classification of the 32 x 32 block (this warp's rows x the chunk's keys):
-        // fully visible blocks take a path without per-key masks
-        const bool none = kc > qhi || qlo - (kc + 31) > p.window;
-        const bool all = (kc + 31 <= qlo) && (qhi - kc <= p.window);
-        // P row r: 16-byte chunk (4c + b) of 8 keys stored at (4c + b) ^ (r % 8) (128-byte swizzle)
-        auto store = [&](int b, const uint32_t (&w)[4]) {
-          *reinterpret_cast<uint4*>(ph + (((4 * c + b) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        };
-        if (all) {
+          for (int c = 0; c < 2; ++c) {
+            const int kc = k0 + 64 * h + 32 * c;
+            // warp-uniform classification of the 32 x 32 block (this warp's rows x the chunk's keys):
+            // fully visible blocks take a path without per-key masks
+            const bool none = kc > qhi || qlo - (kc + 31) > p.window;
+            const bool all = (kc + 31 <= qlo) && (qhi - kc <= p.window);
+            uint32_t pw[16];
+            if (all) {
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            uint32_t w[4];
+              for (int u = 0; u < 16; ++u) {
+                const int i = 32 * c + 2 * u;
+                const float2 x = __ffma2_rn(make_float2(sv[i], sv[i + 1]), kScale2, kNegOffset2);
+                const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                lsum[u & 1] = __fadd2_rn(lsum[u & 1], e);
+                pw[u] = pack_bf16x2(e.x, e.y);
+              }
+            } else if (none) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int i = 32 * c + 8 * b + 2 * u;
-              const float2 x = __ffma2_rn(make_float2(sv[i], sv[i + 1]), kScale2, kNegOffset2);
-              const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-              lsum[u & 1] = __fadd2_rn(lsum[u & 1], e);
-              w[u] = pack_bf16x2(e.x, e.y);
-            }
-            store(b, w);
-          }
-        } else {
+              for (int u = 0; u < 16; ++u) pw[u] = 0u;
+            } else {
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
-            if (!none) {
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int i = 32 * c + 8 * b + 2 * u;
+              for (int u = 0; u < 16; ++u) {
+                const int i = 32 * c + 2 * u;
                 const float2 x = __ffma2_rn(make_float2(sv[i], sv[i + 1]), kScale2, kNegOffset2);
                 float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                const int key = kc + 8 * b + 2 * u;
+                const int key = kc + 2 * u;
                 if (key > q || q - key > p.window) e.x = 0.f;
                 if (key + 1 > q || q - key - 1 > p.window) e.y = 0.f;
                 lsum[u & 1] = __fadd2_rn(lsum[u & 1], e);
-                w[u] = pack_bf16x2(e.x, e.y);
+                pw[u] = pack_bf16x2(e.x, e.y);
               }
             }
-            store(b, w);
+            // P's columns 32h + 16c .. + 15 hold S values this part or the one before it has read
+            tmem_st16(tS + lane_addr + 32 * h + 16 * c, pw);
           }
         }
       }
-      }
-      if (!ok) break;
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g]);
     }
