@@ -13,6 +13,8 @@ Extra keys of the same line, measured in the same process after the headline (sk
   dust                    seconds per DUST update at the speedrun recipe (5,440 draws, config 3) and at
                           24,576 direct draws (config 5), draws split over the GPUs
   eggroll_131072_pairs    (N >= 8) config 5's EGGROLL population: 262,144 members, one update
+  rank_agreement          (N = 1, with the CPU baseline) Spearman rho of 64 members' GPU losses against
+                          the float32 CPU oracle on the same draws, and antithetic-pair sign flips
 
     python bench.py [--gpus N --steps K --warmup W]          # this repository's CUDA path
     python bench.py --impl reference [...]                   # the reference's own ES update on the host cores
@@ -182,6 +184,37 @@ def reference_sample(steps: int = 1, length: int = SEQ):
     return 2 * length, times, cores, 'port', sample
 
 
+def rank_agreement(dev, members: int = 64, length: int = 512):
+    """How the GPU's bf16-operand member losses order members against the float32 CPU oracle on the same
+    counter-based draws (oracle/ restates train/val/eggroll.py:66-103 and is pinned to the reference by
+    tests/golden/population.npz): 64 members = 32 antithetic pairs at sigma 1e-3 on one sequence of 512
+    tokens. Spearman rho of the losses, the pairs whose antithetic difference L[2i+1] - L[2i] changes
+    sign, and the largest oracle |difference| among those (a flip is a near tie within bf16 rounding)."""
+    import numpy as np
+    from noise_b200.data import zipf_tokens
+    from noise_b200.model import Weights
+    from noise_b200.population import population_losses
+    from oracle import eggroll as oe
+    from oracle import model as om
+    rows = zipf_tokens(1, length + 1, seed=17)
+    x, y = rows[:, :-1], rows[:, 1:]
+    pairs, sigma = members // 2, 1e-3
+    got = population_losses(Weights(dev, seed=0), x, y, 0, members, pairs, sigma, 0, 1).cpu().double().numpy()
+    draws, sign = oe.member_draws(np.arange(members), pairs, sigma, 0, 1)
+    with torch.no_grad():
+        want = om.population_losses(om.make_params(0), draws, sign, x, y).double().numpy()
+    rg, rw = np.argsort(np.argsort(got)), np.argsort(np.argsort(want))
+    rho = 1 - 6 * float(np.sum((rg - rw) ** 2)) / (members * (members ** 2 - 1))
+    dg, dw = got[1::2] - got[0::2], want[1::2] - want[0::2]
+    flips = np.sign(dg) != np.sign(dw)
+    return {'members': members, 'tokens': length, 'sigma': sigma, 'spearman': rho, 'pairs': pairs,
+            'pair_sign_flips': int(flips.sum()),
+            'max_flipped_oracle_abs_diff': float(np.abs(dw[flips]).max()) if flips.any() else 0.0,
+            'median_oracle_abs_diff': float(np.median(np.abs(dw))),
+            'max_abs_loss_error': float(np.max(np.abs(got - want))),
+            'checker': 'float32 CPU restatement of population_loss (oracle/)'}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -338,8 +371,12 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tok, times, cores, kind, sample = reference_sample(3, SEQ)
         cpu = {'value': tok / min(times[1:]), 'unit': UNIT, 'cores': cores, 'kind': kind, 'sample': sample}
+        # the oracle's second use here: checking the GPU's member ranking on a small case
+        extras_rank = rank_agreement(dev)
 
     extras = {}
+    if cpu is not None:
+        extras['rank_agreement'] = extras_rank
     if not args.no_extras:
         # one timed update where an update takes tens of seconds (up to 2 GPUs), two above
         extras['fixed_population'] = fixed_population(rank, world, dev, FIXED_MEMBERS, args.sigma, barrier,
