@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
   uint64_t* v_empty = v_full + VS;    // [VS]
   uint64_t* s_full = v_empty + VS;    // [G]
   uint64_t* p_full = s_full + G;      // [G]
-  uint64_t* o_full = p_full + G;
-  uint64_t* drain = o_full + 1;
+  uint64_t* o_full = p_full + G;      // [G]
+  uint64_t* drain = o_full + G;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* bproj = reinterpret_cast<float*>(base + L::kCore + 512);
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
       mbar_init(&s_full[g], 1);
       mbar_init(&p_full[g], 4);
     }
-    mbar_init(o_full, 1);
+    for (int g = 0; g < G; ++g) mbar_init(&o_full[g], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
 #pragma unroll
             for (int k = 0; k < kAtK / 16; ++k)  // 16 keys of P = 8 TMEM columns
               tc_mma_f16_ts(tG + KT, tG + 8 * k, dv + (uint64_t)(2048 >> 4) * k, idesc_o, (jj > lo || k > 0) ? 1u : 0u);
+            if (jj == hi) tc_commit(&o_full[g]);  // this query tile's output is complete
           }
           if (j < n_kt && j >= lo && j <= hi) {
             if (!k_ready) {
@@ -227,7 +228,6 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
         if (jj >= 0) tc_commit(&v_empty[jj % VS]);
         if (j < n_kt) tc_commit(&k_empty[j % KS]);
       }
-      if (ok) tc_commit(o_full);
       tc_commit(drain);
       mbar_wait(drain, 0, abort_flag, status);
     }
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
       if (lane == 0) mbar_arrive(&p_full[g]);
     }
     if (kScore) {
-      if (ok && mbar_wait(o_full, 0, abort_flag, status)) {
+      if (ok && mbar_wait(&o_full[g], 0, abort_flag, status)) {
         tc_fence_after();
         float o[64];
         tmem_ld64(tO + lane_addr, o);
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(AttnTcLayout<G, KT>::kThreads, G == 1 && KT ==
         if (p.base) d -= __ldg(p.base + trow * kHeads + head);
         p.score[(row_base + q) * kHeads + head] = d;
       }
-    } else if (ok && mbar_wait(o_full, 0, abort_flag, status)) {
+    } else if (ok && mbar_wait(&o_full[g], 0, abort_flag, status)) {
       tc_fence_after();
       float o[64];
       tmem_ld64(tO + lane_addr, o);
