@@ -580,19 +580,31 @@ struct EpiMlpOutT {
 
   __device__ void begin_tile(int m_tile, int, int col0) {
     const RowInfo r0 = row_info(p.ctx, (int64_t)m_tile * 128);
-    const uint32_t slot = r0.slot;
-    __syncwarp();
-    warp_draw128(vec, p.ctx, slot, tid_mlp(p.layer), 0, col0, lane);
+    const uint32_t slot = r0.slot, e4 = (col0 >> 2) + lane;
+    // every vector's load is issued before the first store, so the loads overlap one another and the
+    // warp's wait for the previous tile's readers of vec
+    const float4 d_mlp = draw4(p.ctx, slot, tid_mlp(p.layer), 0, e4);
+    float4 d_wte, d_q, d_k, d_v, d_gate;
+    const bool gate = !last && has_ve(p.layer + 1) && col0 == 0 && lane < 8;  // b_gate has 32 entries
     if (!last) {
       const int nl = p.layer + 1;
-      warp_draw128(vec + 128, p.ctx, slot, kTidWte, 1, col0, lane);
-      warp_draw128(vec + 256, p.ctx, slot, tid_q(nl), 1, col0, lane);
-      warp_draw128(vec + 384, p.ctx, slot, tid_k(nl), 1, col0, lane);
-      warp_draw128(vec + 512, p.ctx, slot, tid_v(nl), 1, col0, lane);
-      if (has_ve(nl) && col0 == 0 && lane < 8)  // b_gate has 32 entries
-        reinterpret_cast<float4*>(vec + 640)[lane] = draw4(p.ctx, slot, tid_gate(nl), 1, lane);
+      d_wte = draw4(p.ctx, slot, kTidWte, 1, e4);
+      d_q = draw4(p.ctx, slot, tid_q(nl), 1, e4);
+      d_k = draw4(p.ctx, slot, tid_k(nl), 1, e4);
+      d_v = draw4(p.ctx, slot, tid_v(nl), 1, e4);
+      if (gate) d_gate = draw4(p.ctx, slot, tid_gate(nl), 1, lane);
     } else {
-      warp_draw128(vec + 256, p.ctx, slot, kTidHead, 1, col0, lane);
+      d_q = draw4(p.ctx, slot, kTidHead, 1, e4);
+    }
+    __syncwarp();
+    float4* v4 = reinterpret_cast<float4*>(vec);  // [0] a_mlp, [32] b_wte, [64] b_q or b_head, ...
+    v4[lane] = d_mlp;
+    v4[64 + lane] = d_q;
+    if (!last) {
+      v4[32 + lane] = d_wte;
+      v4[96 + lane] = d_k;
+      v4[128 + lane] = d_v;
+      if (gate) v4[160 + lane] = d_gate;
     }
     __syncwarp();
     if constexpr (kDirect) {
