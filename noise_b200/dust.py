@@ -4,10 +4,13 @@
   rerun(n, entry, jitter) -> noise_pop_forward_direct (orthogonal draws regenerated in-kernel)
   direct_errors           -> noise_dust_errors (centred / discounted rewards contracted with the draws)
   head_error              -> noise_coordinate_differences
-  reassemble              -> one fp32 GEMM (torch.matmul, cuBLAS) per site, as the reference's einsum
+  reassemble              -> noise_reassemble (errT . x on tf32 tensor cores, as the reference's einsum
+                             under set_float32_matmul_precision('high'))
+  CreditMemory            -> torch fp32 algebra (cuBLAS products, cuSOLVER Cholesky) at the same precision
 """
 from __future__ import annotations
 
+import contextlib
 import math
 import re
 from dataclasses import dataclass
@@ -20,6 +23,19 @@ from .population import units_that_fit, workspace, workspace_bytes
 
 HIDDEN = 4 * WIDTH
 SITE_KINDS = {'transformer.wte': 0, 'o': 1, 'attn': 2, 'fc': 3, 'mlp': 4}
+
+
+@contextlib.contextmanager
+def reference_matmul_precision():
+    """torch's fp32 products on TF32 tensor cores while the block runs, as the reference sets for its whole
+    run (train/val/run.py:676: torch.set_float32_matmul_precision('high')); the caller's setting is
+    restored afterwards."""
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision('high')
+    try:
+        yield
+    finally:
+        torch.set_float32_matmul_precision(prev)
 
 
 @dataclass
@@ -530,6 +546,12 @@ class DUST:
 
     @torch.no_grad()
     def step(self, x, y, optimizer) -> float:
+        """One update (run.py:493-542) under the reference's matmul precision: the credit memory's fp32
+        products run as TF32, as in the reference's run."""
+        with reference_matmul_precision():
+            return self._step(x, y, optimizer)
+
+    def _step(self, x, y, optimizer) -> float:
         from .optim import DenseGrad
         self.t += 1
         r, layers = self.recipe, LAYERS

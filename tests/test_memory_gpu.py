@@ -5,6 +5,8 @@
 - the memory (P, S, M, retrievals, alpha) and the whole prior-corrected estimates against the
   reference (tests/golden/memory.npz). The key c comes from the GPU's bf16-GEMM logits, so the memory
   is compared by relative L2 (<= 3e-2 for P and S, 5e-2 for M, retrievals and estimates) and cosine.
+  The memory's products run on TF32, the precision DUST.step gives them (the reference's run sets
+  set_float32_matmul_precision('high'), train/val/run.py:676; the fixture was made on the CPU in fp32).
   The MLP hidden site is held to the oracle run with the GPU's own live-unit mask (same bounds); against
   the reference only its cosine is checked, since ~0.2% of units are live in one forward and not the
   other and the prior's predicted drop sums over all of a token's units.
@@ -37,6 +39,13 @@ def _pick(f, key, flat):
     if key in f:
         return flat, torch.from_numpy(f[key]).reshape(-1).double()
     return flat[torch.from_numpy(f[key + '__idx'])], torch.from_numpy(f[key + '__val'])
+
+
+@pytest.fixture(scope='module', autouse=True)
+def _reference_precision():
+    from noise_b200.dust import reference_matmul_precision
+    with reference_matmul_precision():
+        yield
 
 
 @pytest.fixture(scope='module')
