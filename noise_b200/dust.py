@@ -201,6 +201,7 @@ class CreditMemory:
         self.S, self.alpha, self.calibration, self.fits, self.estimates = {}, {}, {}, {}, {}
         self._chol = None
         self._chol_of = None
+        self._M = {}
 
     def _average(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
@@ -209,7 +210,10 @@ class CreditMemory:
         return t
 
     def matrix(self, name: str) -> torch.Tensor | None:
-        """M = S (P + ridge mean(diag P) I)^-1; one factorisation serves every site (run.py:281-292)."""
+        """M = S (P + ridge mean(diag P) I)^-1; one factorisation serves every site (run.py:281-292).
+        P and S change only in remember(), so the first call after it solves for every site with a
+        memory at once: one triangular solve whose right-hand sides are all the sites' S^T columns (each
+        column is solved on its own, as in a solve per site), instead of one narrow solve per site."""
         S = self.S.get(name)
         if S is None:
             return None
@@ -218,7 +222,16 @@ class CreditMemory:
             eye = torch.eye(len(self.P), dtype=self.P.dtype, device=self.P.device)
             self._chol = torch.linalg.cholesky(self.P + lam * eye)
             self._chol_of = self.P
-        return torch.cholesky_solve(S.T, self._chol).T
+            self._M = {}
+        if name not in self._M:
+            names = [n for n in self.S if n not in self._M]
+            sol = torch.cholesky_solve(torch.cat([self.S[n].T for n in names], dim=1), self._chol)
+            off = 0
+            for n in names:
+                d = self.S[n].shape[0]
+                self._M[n] = sol[:, off:off + d].T
+                off += d
+        return self._M[name]
 
     def retrieve(self, credit: torch.Tensor, names: list[str]) -> dict:
         """{site: M c [B*T, d]} for the sites with a memory (run.py:294-302); credit is [B*T, 4096]."""
