@@ -155,7 +155,9 @@ int noise_coordinate_differences(const float* raw, const int32_t* targets, int64
  * with x's rows first scaled by 1 / rms(x[k][0 .. x_ld)) when x_norm (the normalised module inputs of
  * mlp.c_fc, lm_head and the attention projections; `in` may be narrower than x_ld, as for ve_gate's
  * first 32 channels). out % 128 == 0, in % 256 == 0 and K % 32 == 0 run on tf32 tensor cores (the
- * reference's float32 einsum under 'high' matmul precision); other shapes in fp32 on CUDA cores. */
+ * reference's float32 einsum under 'high' matmul precision), K split into blocks whose partial
+ * products the workspace holds and that are added in order; other shapes in fp32 on CUDA cores. The
+ * workspace size depends on the shape only. */
 int64_t noise_reassemble_workspace_bytes(int K, int out, int in);
 int noise_reassemble(const float* err, int err_ld, int K, int out, const void* x, int x_bf16, int x_ld, int in,
                      int x_norm, float* g, void* workspace, size_t workspace_bytes, int* status, void* stream);
