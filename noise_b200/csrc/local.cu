@@ -166,18 +166,19 @@ struct LocalCredit {
   float gamma, tail;   // tail = gamma^(window + 1)
 };
 
-// One warp per (row block z, head). credit(t) = c(t) + gamma credit(t + 1) with
-// c(t) = score(t) - gamma^(window+1) score(t + window + 1): each lane runs the recurrence over its
-// T / 32 tokens, a shuffle scan over the lanes carries the tails in, and a second pass adds them.
+// One CTA per row block z; T is cut into 32 chunks of L = T / 32 tokens. Thread (warp w, lane l)
+// takes head l % 8 of chunk 4 w + l / 8, so that each load of a warp reads the 8 heads of one token
+// (32 contiguous bytes) in each of 4 chunks. credit(t) = c(t) + gamma credit(t + 1) with
+// c(t) = score(t) - gamma^(window+1) score(t + window + 1): every thread runs the recurrence over its
+// chunk from zero, one thread per head carries the chunks' start values back through the chunks in
+// shared memory, and a second pass adds gamma^(chunk end - t) times the carry of the next chunk.
 __global__ void __launch_bounds__(256) local_credit_kernel(const __grid_constant__ LocalCredit p) {
-  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (wid >= (int64_t)p.Z * kHeads) return;
-  const int lane = threadIdx.x & 31;
-  const int64_t z = wid / kHeads;
-  const int head = (int)(wid % kHeads);
+  __shared__ float start[kHeads][32], carry[kHeads][32];
+  const int64_t z = blockIdx.x;
+  const int head = threadIdx.x & 7, chunk = threadIdx.x >> 3;
   const float* s = p.score + z * p.T * kHeads + head;
   float* o = p.out + z * p.T * kHeads + head;
-  const int L = p.T / 32, t0 = lane * L;
+  const int L = p.T / 32, t0 = chunk * L;
   float y = 0.f;
   for (int t = t0 + L - 1; t >= t0; --t) {
     float c = s[(int64_t)t * kHeads];
@@ -185,21 +186,24 @@ __global__ void __launch_bounds__(256) local_credit_kernel(const __grid_constant
     y = c + p.gamma * y;
     o[(int64_t)t * kHeads] = y;
   }
-  float gL = 1.f;
-  for (int i = 0; i < L; ++i) gL *= p.gamma;
-  float Y = y, g = gL;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const float v = __shfl_down_sync(0xffffffffu, Y, off);
-    if (lane + off < 32) Y += g * v;
-    g *= g;
+  start[head][chunk] = y;
+  __syncthreads();
+  if (threadIdx.x < kHeads) {  // thread h: carry[h][k] = credit at the first token of chunk k + 1
+    float gL = 1.f;
+    for (int i = 0; i < L; ++i) gL *= p.gamma;
+    float c = 0.f;
+    carry[threadIdx.x][31] = 0.f;
+    for (int k = 30; k >= 0; --k) {
+      c = start[threadIdx.x][k + 1] + gL * c;
+      carry[threadIdx.x][k] = c;
+    }
   }
-  float carry = __shfl_down_sync(0xffffffffu, Y, 1);
-  if (lane == 31) carry = 0.f;
+  __syncthreads();
+  const float cr = carry[head][chunk];
   float f = 1.f;
   for (int t = t0 + L - 1; t >= t0; --t) {
     f *= p.gamma;
-    o[(int64_t)t * kHeads] += f * carry;
+    o[(int64_t)t * kHeads] += f * cr;
   }
 }
 
@@ -376,7 +380,7 @@ extern "C" int noise_local_errors(const NoiseLocal* s, const float* rope, int B,
     lc.gamma = s->gamma;
     lc.tail = (float)pow((double)s->gamma, (double)(lc.window + 1));
     LaunchScope scope(kKindOther, st);
-    local_credit_kernel<<<(unsigned)(((int64_t)lc.Z * kHeads * 32 + 255) / 256), 256, 0, st>>>(lc);
+    local_credit_kernel<<<(unsigned)lc.Z, 256, 0, st>>>(lc);
     if (cudaGetLastError() != cudaSuccess) return kStatusLaunchFailed;
     w = credit;
   }
