@@ -176,7 +176,7 @@ class ShardedOptimizer:
         `scale` (1 / world for the reference's average, train/val/run.py:536, average_ranks at :154-158), each rank steps its
         region and the all-gather restores the model. The reference checks the averaged gradient for
         non-finite values before stepping (:537-538); here every rank checks its summed region and the
-        verdict is all-reduced, so all ranks skip together. Returns False (nothing stepped) on a
+        result is all-reduced, so all ranks skip together. Returns False (nothing stepped) on a
         non-finite gradient."""
         plan = self.plan
         for r in range(self.world):
